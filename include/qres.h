@@ -1,0 +1,194 @@
+/*
+ * libqres -- the resident decode step of a Qwen3.6-27B-shaped hybrid model (48 Gated DeltaNet + 16 gated
+ * full-attention layers) as hand-written sm_100a CUDA kernels behind a plain C ABI.
+ *
+ * It replaces the device side of sott0n/tt-qwen-resident's decode path: the per-chip resident program that
+ * ``ResidentModel`` builds (qwen36_resident/model.py:403-1299) and launches with ``ttnn.generic_op`` /
+ * ``ttnn.execute_trace`` (model.py:1485-1508), and the kernels under qwen36_resident/kernels/.
+ *
+ * Conventions: every function returns a qres_status (0 = ok) and never throws; on failure the context keeps a
+ * message for qres_last_error. Device memory is allocated by the caller (e.g. torch) and passed as raw
+ * pointers; the library never frees caller memory. Work is stream-ordered on the caller's stream (a
+ * cudaStream_t passed as void*). One context per rank (process).
+ */
+#ifndef QRES_H_
+#define QRES_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QRES_API __attribute__((visibility("default")))
+#else
+#define QRES_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    QRES_OK = 0,
+    QRES_ERR_ARG = 1,    /* bad argument / shape / unbound buffer */
+    QRES_ERR_CUDA = 2,   /* a CUDA runtime call failed */
+    QRES_ERR_DEVICE = 3, /* a kernel reported an error word (bounded wait ran out, index out of range) */
+    QRES_ERR_STATE = 4,  /* call out of order (e.g. replay without a captured graph) */
+    QRES_ERR_COMM = 5    /* the tensor-parallel exchange failed */
+} qres_status;
+
+/* projection kinds (the weight entries of model.py:582-589) */
+typedef enum {
+    QRES_W_GDN_IN = 0,  /* [q|k|v|z|a|b] rows of the rank's GDN heads, K = 5120 */
+    QRES_W_ATTN_IN = 1, /* [q|gate|k|v] rows of the rank's attention heads, K = 5120 */
+    QRES_W_OUT = 2,     /* out-projection, 5120 rows, K = 6144 / nranks (row-parallel) */
+    QRES_W_GATEUP = 3,  /* gate|up rows interleaved in pairs (g0 g1 u0 u1 ...), K = 5120 */
+    QRES_W_DOWN = 4,    /* down-projection, 5120 rows, K = 17408 / nranks (row-parallel) */
+    QRES_W_HEAD = 5     /* lm_head rows of the rank's vocab slice, K = 5120 */
+} qres_weight_kind;
+
+#define QRES_MAX_ROWS 8    /* users (or verify rows) per step */
+#define QRES_HIST_SLOTS 8  /* conv-history ring slots per user: position p lives in slot p % 8 */
+#define QRES_KV_BLOCK 64   /* positions per KV page */
+#define QRES_TOPK 32       /* candidates per list (sampling.hpp kTopK) */
+
+/* model / launch configuration (the shape arguments of ResidentModel, model.py:404-420) */
+typedef struct {
+    int32_t layers;        /* decoder layers per step */
+    int32_t attn_interval; /* layer l is full attention when interval > 0 && (l + 1) % interval == 0 */
+    int32_t vocab;         /* lm_head rows over all ranks; 0 = no lm_head */
+    int32_t rows;          /* users per step, 1..QRES_MAX_ROWS */
+    int32_t max_pages;     /* page-table entries per user */
+    int32_t num_pages;     /* pages in each attention layer's K (and V) pool */
+    int32_t sm_count;      /* CTAs of the weight-streaming kernels; 0 = the device's SM count */
+    int32_t flags;         /* reserved, 0 */
+} qres_config;
+
+/* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block), in the GEMV layout made by
+ * qres_tile_weight: rows in quads of 4, each quad's K split into chunks of 512, a chunk stored as its 4 rows
+ * back to back. sidx maps every (padded) row to its row of the scale table. */
+typedef struct {
+    const void* data;      /* rows_pad * K bytes */
+    const float* scales;   /* [n_scale_rows][K / 128] */
+    const int32_t* sidx;   /* [rows_pad], non-decreasing */
+    int32_t rows;          /* real rows */
+    int32_t rows_pad;      /* rows rounded up to a multiple of 4 */
+    int32_t K;             /* multiple of 128 */
+    int32_t n_scale_rows;
+} qres_weight;
+
+/* per-layer decode state (State, model.py:151-174), laid out for this rank */
+typedef struct {
+    float* gdn_state;     /* GDN layer: [rows][48/n][128][128] fp32, updated in place */
+    uint16_t* conv_hist;  /* GDN layer: [rows][QRES_HIST_SLOTS][conv_ch/n] bf16 */
+    uint16_t* k_pool;     /* attention layer: [num_pages][kv_heads_local][64][256] bf16 */
+    uint16_t* v_pool;     /* attention layer: same */
+} qres_layer_state;
+
+/* the token state of a step (model.py:1314-1351 / streamer_common.hpp:227-230), in device memory */
+typedef struct {
+    int32_t pos[QRES_MAX_ROWS];   /* position of each row */
+    int32_t token[QRES_MAX_ROWS]; /* token id of each row (embedding gather); < 0: take the row of x0 */
+    int32_t feed;                 /* 1: the step writes its greedy token and pos + 1 back here */
+    int32_t step;                 /* incremented by every step (device side) */
+    int32_t reserved[14];
+} qres_tok;
+
+/* per-step inputs and outputs (device pointers) */
+typedef struct {
+    qres_tok* tok;
+    const float* x0;        /* [rows][5120] fp32 (bf16 values), used where tok.token < 0 */
+    const uint16_t* embed;  /* [vocab][5120] bf16, or NULL */
+    const int32_t* page_table; /* [rows][max_pages] */
+    float* x;               /* [rows][5120] residual stream; x after the last layer when the step ends */
+    uint16_t* logits;       /* [rows][vocab / n] bf16 (lm_head) */
+    uint32_t* topk;         /* [rows][2 * QRES_TOPK] this rank's list: keys, then vocab indices (lm_head) */
+    int32_t* out;           /* [rows][4]: greedy token, position, 0, 0 (lm_head) */
+    uint16_t* mixer_out;    /* [rows][6144 / n] bf16 copy of the last layer's mixer output, or NULL */
+} qres_io;
+
+typedef struct qres_ctx qres_ctx;
+
+/* ---- context ---- */
+/* Replaces ResidentModel.__init__'s program build (model.py:403-1299) for one rank of nranks. */
+QRES_API qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qres_ctx** out);
+QRES_API qres_status qres_destroy(qres_ctx* ctx);
+/* The last error message of the context (or of the library when ctx is NULL). */
+QRES_API qres_status qres_last_error(const qres_ctx* ctx, char* buf, size_t len);
+
+/* ---- binding (the DRAM tensors ResidentModel places: weights model.py:574-605, state :623-760) ---- */
+/* Projection `kind` of `layer` (QRES_W_HEAD: layer ignored). Binds pointers; nothing is copied. */
+QRES_API qres_status qres_load_weights(qres_ctx* ctx, int32_t layer, int32_t kind, const qres_weight* w);
+/* GDN layer parameters: conv taps [conv_ch/n][4] bf16 (tap 0 = oldest), dt_bias and neg_A [48/n] fp32,
+ * gated-norm weight [128] fp32 (weights.py:162-189). */
+QRES_API qres_status qres_load_gdn_params(qres_ctx* ctx, int32_t layer, const uint16_t* taps, const float* dt,
+                                 const float* neg_a, const float* norm_w);
+/* Attention layer parameters: q-norm weight already divided by sqrt(256), k-norm weight, [256] fp32 each
+ * (model.py:237-238). */
+QRES_API qres_status qres_load_attn_params(qres_ctx* ctx, int32_t layer, const float* wq, const float* wk);
+/* Per-layer decode state buffers (State, model.py:151-174; load_state :1447-1470 writes their contents). */
+QRES_API qres_status qres_bind_state(qres_ctx* ctx, int32_t layer, const qres_layer_state* st);
+/* Rope tables [max_pos][32] fp32 cos and sin of model.py:128-131 (fp64 angles rounded to fp32). */
+QRES_API qres_status qres_bind_rope(qres_ctx* ctx, const float* cos_tab, const float* sin_tab, int32_t max_pos);
+QRES_API qres_status qres_bind_io(qres_ctx* ctx, const qres_io* io);
+/* Scratch the step needs (activations, split-K partials, counters, the error word). */
+QRES_API qres_status qres_workspace_size(const qres_ctx* ctx, size_t* bytes);
+QRES_API qres_status qres_bind_workspace(qres_ctx* ctx, void* dev, size_t bytes);
+
+/* ---- tensor parallelism ---- */
+/* The row-parallel all-reduces after the out- and down-projections (mlp_hub.cpp:309-364) and the top-k
+ * exchange after the lm_head (mlp_hub.cpp:366-411) run over NCCL for nranks > 1. Rank 0 makes an id
+ * (128 bytes) with qres_nccl_unique_id, the caller broadcasts it, every rank calls qres_nccl_init. libpath: the
+ * libnccl.so.2 to load (NULL: the one already loaded in the process, else the default search). */
+QRES_API qres_status qres_nccl_unique_id(const char* libpath, void* id128);
+QRES_API qres_status qres_nccl_init(qres_ctx* ctx, const char* libpath, const void* id128);
+
+/* ---- the step (ResidentModel.step, model.py:1499-1508) ---- */
+/* Enqueue one decode step on `stream`. */
+QRES_API qres_status qres_decode_step(qres_ctx* ctx, void* stream);
+/* capture_trace / step-with-trace / release_trace (model.py:1485-1505) as a CUDA graph of one step. */
+QRES_API qres_status qres_capture(qres_ctx* ctx, void* stream);
+QRES_API qres_status qres_replay(qres_ctx* ctx, void* stream);
+QRES_API qres_status qres_release_graph(qres_ctx* ctx);
+/* Synchronise `stream` and read the device error word; QRES_ERR_DEVICE (with a message) when a kernel of the
+ * step reported a timeout or an out-of-range index. The word is cleared. */
+QRES_API qres_status qres_check(qres_ctx* ctx, void* stream);
+/* Kernel launches enqueued by the last qres_decode_step. */
+QRES_API int32_t qres_step_launches(const qres_ctx* ctx);
+
+/* ---- single kernels (the building blocks of a step, for tests and microbenchmarks) ---- */
+/* y = act(h @ W^T) for `rows` users: pro 0 = h = bf16(rmsnorm(x)) from fp32 x [rows][K]; pro 1 = h = bf16
+ * input [rows][K]. epi 0 = bf16 out [rows][w.rows]; 1 = SwiGLU over interleaved gate|up pairs, bf16 out
+ * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid 0 = the SM count. */
+QRES_API qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
+                      int32_t grid, uint32_t* err, void* stream);
+/* One GDN mixer (streamer conv1d+SiLU model.py:255-258 and gdn_head_compute.cpp) for `rows` users at the
+ * positions in pos[] (device): y [rows][ld_y] in-projection rows -> o [rows][6144/n] bf16. */
+QRES_API qres_status qres_gdn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int32_t ld_y, const int32_t* pos,
+                           const uint16_t* taps, const float* dt, const float* neg_a, const float* norm_w,
+                           float* state, uint16_t* conv_hist, uint16_t* o, uint32_t* err, void* stream);
+/* One gated-attention mixer (model.py:233-247) over the paged KV cache: y [rows][ld_y] -> o [rows][6144/n]
+ * bf16; appends each row's k / v at its position. work: qres_attn_workspace_size bytes, zeroed once before
+ * first use (the kernel leaves it reusable). */
+QRES_API qres_status qres_attn_workspace_size(int32_t nranks, int32_t rows, int32_t max_pos, size_t* bytes);
+QRES_API qres_status qres_attn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int32_t ld_y, const int32_t* pos,
+                            const int32_t* page_table, int32_t max_pages, const float* wq, const float* wk,
+                            const float* cos_tab, const float* sin_tab, uint16_t* k_pool, uint16_t* v_pool,
+                            uint16_t* o, void* work, size_t work_bytes, uint32_t* err, void* stream);
+/* Per-row top-32 list (keys, then indices; sampling.hpp:24-74 order and tie rule) and argmax of bf16 logits
+ * [rows][n_logits] whose first element is vocab index `base` (streamer_writer.cpp:451-500 + the hub's merge).
+ * work: qres_topk_workspace_size bytes, zeroed once before first use (the kernel leaves it reusable). */
+QRES_API qres_status qres_topk_workspace_size(int32_t rows, int32_t n_logits, size_t* bytes);
+QRES_API qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base, uint32_t* lists,
+                      int32_t* argmax, void* work, size_t work_bytes, void* stream);
+
+/* ---- weight preparation ---- */
+/* fp32 [N][K] -> e4m3 bytes [N][K] + scales [ceil(N/128)][K/128] (amax / 448 per 128 x 128 block). */
+QRES_API qres_status qres_quantize_fp8(const float* w, int32_t N, int32_t K, uint8_t* q, float* scales, void* stream);
+/* row-major e4m3 [rows][K] -> the GEMV layout of qres_weight (rows_pad = rows rounded up to 4, zero rows). */
+QRES_API qres_status qres_tile_weight(const uint8_t* src, int32_t rows, int32_t K, uint8_t* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRES_H_ */

@@ -125,6 +125,62 @@ class Prepared:
             self.head = [T(w.head[s.vocab_rows(V)]) for s in self.sh]
 
 
+def gdn_mixer(y, s, taps, wg, hist, S_all):
+    """the GDN mixer of rank s (model.py:255-276): y the rank's bf16 in-projection row [q|k|v|z|a|b], taps its
+    conv taps [conv, 4], wg the layer's dt / neg_a [48] and norm_w, hist [3, conv] (inputs at pos-3..pos-1),
+    S_all the layer's states [48, 128, 128] (the rank's heads updated in place). Returns (o, new hist)."""
+    conv_l = 2 * s.gq + s.gv
+    window = torch.cat([hist, y[:conv_l][None]], 0)  # oldest first
+    conv = bf16(F.silu((window * taps.T).sum(0)))
+    q, k, v = conv[: s.gq], conv[s.gq : 2 * s.gq], conv[2 * s.gq : conv_l]
+    z0 = conv_l
+    a0 = z0 + s.gv
+    b0 = a0 + s.nv
+    z, a, b = y[z0:a0], y[a0:b0], y[b0 : b0 + s.nv]
+    scale = DK**-0.5
+    outs = []
+    for hh in range(s.nv):
+        g_h = s.r * s.nv + hh  # global value head
+        kh = hh // (s.nv // s.nk)
+        qn = q[kh * DK : (kh + 1) * DK]
+        qn = qn * torch.rsqrt(qn.pow(2).sum() + 1e-6) * scale
+        kn = k[kh * DK : (kh + 1) * DK]
+        kn = kn * torch.rsqrt(kn.pow(2).sum() + 1e-6)
+        decay = torch.exp(wg["neg_a"][g_h] * F.softplus(a[hh] + wg["dt"][g_h]))
+        beta = torch.sigmoid(b[hh])
+        S = S_all[g_h]
+        delta = beta * (v[hh * DV : (hh + 1) * DV] - (decay * kn) @ S)
+        S = decay * S + torch.outer(kn, delta)
+        S_all[g_h] = S
+        on = rmsnorm(qn @ S, wg["norm_w"])
+        outs.append(bf16(on * F.silu(z[hh * DV : (hh + 1) * DV])))
+    return torch.cat(outs), window[1:]
+
+
+def attn_mixer(y, s, wq, wk, K_all, V_all, pos, cos, sin):
+    """the gated-attention mixer of rank s (model.py:233-247): y the rank's bf16 row [q|gate|k|v], K_all /
+    V_all the layer's caches [4, max_pos, 256] (row pos of the rank's KV heads written). Returns o (bf16)."""
+    aq = s.h * HD
+    q = y[:aq].view(s.h, HD)
+    gate = y[aq : 2 * aq].view(s.h, HD)
+    k = y[2 * aq : 2 * aq + s.nkv * HD].view(s.nkv, HD)
+    v = y[2 * aq + s.nkv * HD :].view(s.nkv, HD)
+    qn = rope(rmsnorm(q, wq / math.sqrt(HD)), cos, sin)
+    kn = bf16(rope(rmsnorm(k, wk), cos, sin))
+    group = s.h // s.nkv
+    outs = []
+    for j in range(s.nkv):
+        kvh = s.kv0 + j
+        K = torch.cat([K_all[kvh][:pos], kn[j][None]])
+        V = torch.cat([V_all[kvh][:pos], v[j][None]])
+        qj = qn[j * group : (j + 1) * group]
+        p = torch.softmax(qj @ K.T, dim=-1)
+        outs.append(bf16((p @ V) * torch.sigmoid(gate[j * group : (j + 1) * group])).flatten())
+        K_all[kvh][pos] = kn[j]
+        V_all[kvh][pos] = v[j]
+    return torch.cat(outs)
+
+
 def torch_step(x0, P, st, layers, interval, lm_head=False, mixer_out=None):
     """one decode step of one user at st.pos over Prepared weights P; updates st (GDN states, conv histories,
     KV rows at pos) in place and returns x (and the per-rank logits with lm_head). mixer_out: a list that
@@ -141,26 +197,8 @@ def torch_step(x0, P, st, layers, interval, lm_head=False, mixer_out=None):
             c = a_i % len(w.attn)
             wa = w.attn[c]
             for r, s in enumerate(P.sh):
-                aq = s.h * HD
                 y = bf16(h @ P.attn[c][r])
-                q = y[:aq].view(s.h, HD)
-                gate = y[aq : 2 * aq].view(s.h, HD)
-                k = y[2 * aq : 2 * aq + s.nkv * HD].view(s.nkv, HD)
-                v = y[2 * aq + s.nkv * HD :].view(s.nkv, HD)
-                qn = rope(rmsnorm(q, wa["wq"] / math.sqrt(HD)), cos, sin)
-                kn = bf16(rope(rmsnorm(k, wa["wk"]), cos, sin))
-                group = s.h // s.nkv
-                outs = []
-                for j in range(s.nkv):
-                    kvh = s.kv0 + j
-                    K = torch.cat([st.K[c][kvh][:pos], kn[j][None]])
-                    V = torch.cat([st.V[c][kvh][:pos], v[j][None]])
-                    qj = qn[j * group : (j + 1) * group]
-                    p = torch.softmax(qj @ K.T, dim=-1)
-                    outs.append(bf16((p @ V) * torch.sigmoid(gate[j * group : (j + 1) * group])).flatten())
-                    st.K[c][kvh][pos] = kn[j]
-                    st.V[c][kvh][pos] = v[j]
-                o = torch.cat(outs)
+                o = attn_mixer(y, s, wa["wq"], wa["wk"], st.K[c], st.V[c], pos, cos, sin)
                 if mixer_out is not None:
                     mixer_out.append((l, r, o))
                 parts.append(o @ P.out[l % len(w.out)][r] + (x if r == 0 else 0))
@@ -168,37 +206,11 @@ def torch_step(x0, P, st, layers, interval, lm_head=False, mixer_out=None):
         else:
             c = g_i % len(w.gdn)
             wg = w.gdn[c]
-            scale = DK**-0.5
             for r, s in enumerate(P.sh):
                 y = bf16(h @ P.gdn[c][r]["Win"])
-                conv_l = 2 * s.gq + s.gv
                 ch = s.conv_channels()
                 hist = st.hist[c][:, ch]
-                window = torch.cat([hist, y[:conv_l][None]], 0)  # oldest first
-                st.hist[c][:, ch] = window[1:]
-                conv = bf16(F.silu((window * P.gdn[c][r]["taps"].T).sum(0)))
-                q, k, v = conv[: s.gq], conv[s.gq : 2 * s.gq], conv[2 * s.gq : conv_l]
-                z0 = conv_l
-                a0 = z0 + s.gv
-                b0 = a0 + s.nv
-                z, a, b = y[z0:a0], y[a0:b0], y[b0 : b0 + s.nv]
-                outs = []
-                for hh in range(s.nv):
-                    g_h = s.r * s.nv + hh  # global value head
-                    kh = hh // (s.nv // s.nk)
-                    qn = q[kh * DK : (kh + 1) * DK]
-                    qn = qn * torch.rsqrt(qn.pow(2).sum() + 1e-6) * scale
-                    kn = k[kh * DK : (kh + 1) * DK]
-                    kn = kn * torch.rsqrt(kn.pow(2).sum() + 1e-6)
-                    decay = torch.exp(wg["neg_a"][g_h] * F.softplus(a[hh] + wg["dt"][g_h]))
-                    beta = torch.sigmoid(b[hh])
-                    S = st.gdn[c][g_h]
-                    delta = beta * (v[hh * DV : (hh + 1) * DV] - (decay * kn) @ S)
-                    S = decay * S + torch.outer(kn, delta)
-                    st.gdn[c][g_h] = S
-                    on = rmsnorm(qn @ S, wg["norm_w"])
-                    outs.append(bf16(on * F.silu(z[hh * DV : (hh + 1) * DV])))
-                o = torch.cat(outs)
+                o, st.hist[c][:, ch] = gdn_mixer(y, s, P.gdn[c][r]["taps"], wg, hist, st.gdn[c])
                 if mixer_out is not None:
                     mixer_out.append((l, r, o))
                 parts.append(o @ P.out[l % len(w.out)][r] + (x if r == 0 else 0))

@@ -1,0 +1,396 @@
+// Small kernels of the decode step and weight preparation for sm_100a:
+//  - tile_weight: row-major e4m3 [rows][K] -> the GEMV quad/chunk layout (gemv_fp8.cu);
+//  - quantize_fp8: fp32 [N][K] -> e4m3 + one fp32 scale per 128 x 128 block (amax / 448);
+//  - topk: per-row top-32 (key, index) list and argmax of bf16 logits, the order and tie rule of the
+//    reference's sampling.hpp (:24-74): bf16 order keys descending, the smaller vocab index first on ties;
+//  - embed_rows: the step's input rows, x0 or embed[token] (streamer_reader.cpp:117-128);
+//  - feed: the device-fed next token state (mlp_hub.cpp:414-458): token = greedy pick, pos + 1.
+#include "qres_common.cuh"
+
+namespace qres {
+
+// ------------------------------------------------------------------------------------------------ tiling
+__global__ void tile_weight_kernel(const uint8_t* __restrict__ src, int rows, int K, uint8_t* __restrict__ dst,
+                                   size_t total16) {
+    // one 16-byte vector of the destination per thread
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < total16; v += (size_t)gridDim.x * blockDim.x) {
+        const size_t off = v * 16;
+        const size_t quad = off / (4 * (size_t)K);
+        const size_t rem = off % (4 * (size_t)K);
+        const int c = (int)(rem / 2048);
+        const int wc = min(512, K - c * 512);
+        const int inner = (int)(rem - (size_t)c * 2048);
+        const int r = inner / wc, i = inner % wc;
+        const size_t row = quad * 4 + r;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)c * 512 + i);
+        *reinterpret_cast<uint4*>(dst + off) = val;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ quantize
+__global__ void quantize_fp8_kernel(const float* __restrict__ w, int N, int K, uint8_t* __restrict__ q,
+                                    float* __restrict__ scales) {
+    const int nb = blockIdx.y, kb = blockIdx.x;
+    const int kbs = (K + 127) / 128;
+    __shared__ float red[8];
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) {
+        const int r = nb * 128 + i / 128, c = kb * 128 + i % 128;
+        if (r < N && c < K) amax = fmaxf(amax, fabsf(w[(size_t)r * K + c]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    const float scale = m > 0.f ? m / 448.0f : 1.0f;
+    if (threadIdx.x == 0) scales[(size_t)nb * kbs + kb] = scale;
+    for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) {
+        const int r = nb * 128 + i / 128, c = kb * 128 + i % 128;
+        if (r < N && c < K) {
+            const float v = __fdiv_rn(w[(size_t)r * K + c], scale);
+            q[(size_t)r * K + c] = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ top-k
+constexpr int kTopK = QRES_TOPK;
+constexpr int kTopkThreads = 512;
+
+__device__ __forceinline__ uint32_t key_of_bf16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
+
+// Select the top-32 of n candidates (key in [0, 65535], distinct indices) held in shared memory, in
+// (key desc, index asc) order, into out_k / out_i. Radix select on the 16-bit key (high byte, then low byte),
+// then the elements above the threshold plus the lowest-index ones equal to it, then a sort of those <= 32.
+// All threads of the block call it.
+__device__ void block_top32(const uint16_t* keys, const uint32_t* idx, int n, uint32_t* out_k, uint32_t* out_i,
+                            int* hist, int* scratch) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    // pass 1: high byte
+    for (int i = tid; i < 256; i += nt) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) atomicAdd(&hist[keys[i] >> 8], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0, bin = -1;
+        for (int b = 255; b >= 0; --b) {
+            if (acc + hist[b] >= kTopK) {
+                bin = b;
+                break;
+            }
+            acc += hist[b];
+        }
+        scratch[0] = bin;  // -1: fewer than 32 candidates, take all
+        scratch[1] = acc;  // count above the bin
+    }
+    __syncthreads();
+    const int hb = scratch[0];
+    int T = -1;  // threshold key: everything > T is in, == T partially
+    if (hb >= 0) {
+        for (int i = tid; i < 256; i += nt) hist[i] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += nt)
+            if ((keys[i] >> 8) == hb) atomicAdd(&hist[keys[i] & 0xff], 1);
+        __syncthreads();
+        if (tid == 0) {
+            int acc = scratch[1], lb = 0;
+            for (int b = 255; b >= 0; --b) {
+                if (acc + hist[b] >= kTopK) {
+                    lb = b;
+                    break;
+                }
+                acc += hist[b];
+            }
+            scratch[2] = (hb << 8) | lb;
+            scratch[3] = acc;  // count strictly above T
+        }
+        __syncthreads();
+        T = scratch[2];
+    }
+    // gather: key > T (any order), then key == T by ascending index (block prefix over index order)
+    __shared__ uint64_t cand[kTopK];
+    __shared__ int ncand;
+    if (tid == 0) ncand = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
+        if ((int)keys[i] > T) {
+            const int s = atomicAdd(&ncand, 1);
+            cand[s] = ((uint64_t)keys[i] << 32) | (0xffffffffu - idx[i]);
+        }
+    }
+    __syncthreads();
+    if (T >= 0) {
+        const int above = ncand, need = kTopK - above;
+        // equal keys: the `need` smallest indices (indices ascend with position in these arrays). Each thread
+        // owns a contiguous segment; an exclusive scan of the per-segment counts gives every equal element its
+        // rank in index order.
+        const int seg = (n + nt - 1) / nt;
+        const int a0 = min(tid * seg, n), a1 = min(a0 + seg, n);
+        int cnt = 0;
+        for (int i = a0; i < a1; ++i) cnt += (int)keys[i] == T;
+        const int lane = tid & 31, warp = tid >> 5;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        __shared__ int wsum[32];
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        int wbase = 0;
+        for (int w = 0; w < warp; ++w) wbase += wsum[w];
+        int r = wbase + incl - cnt;
+        for (int i = a0; i < a1 && r < need; ++i) {
+            if ((int)keys[i] == T) {
+                cand[above + r] = ((uint64_t)T << 32) | (0xffffffffu - idx[i]);
+                ++r;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) ncand = kTopK;
+        __syncthreads();
+    }
+    // sort <= 32 candidates descending (one warp, bitonic over 32 lanes)
+    if (tid < 32) {
+        uint64_t v = tid < ncand ? cand[tid] : 0ull;  // empty: key 0, index 0xffffffff
+        for (int k = 2; k <= 32; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+                const bool up = ((tid & k) == 0);  // descending overall
+                const bool lower = (tid & j) == 0;
+                const uint64_t mx = v > o ? v : o, mn = v > o ? o : v;
+                v = (lower == up) ? mx : mn;
+            }
+        }
+        out_k[tid] = (uint32_t)(v >> 32);
+        out_i[tid] = 0xffffffffu - (uint32_t)(v & 0xffffffffu);
+    }
+    __syncthreads();
+}
+
+struct TopkParams {
+    const uint16_t* logits;
+    int n, ld, base, rows;
+    uint32_t* cand;       // [rows][nblk][64]
+    int* ticket;          // [rows]
+    uint32_t* lists;      // [rows][64] keys then indices
+    int32_t* argmax;      // [rows] or null
+    int nblk;
+};
+
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const TopkParams p) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int blk = blockIdx.x, row = blockIdx.y;
+    const int per = (p.n + p.nblk - 1) / p.nblk;
+    const int lo = blk * per, hi = min(lo + per, p.n);
+    const int cnt = max(hi - lo, 0);
+    uint16_t* keys = reinterpret_cast<uint16_t*>(sm);
+    const int cap = max(per, p.nblk * kTopK);
+    uint32_t* idx = reinterpret_cast<uint32_t*>(sm + ((cap * 2 + 15) & ~15));
+    __shared__ int hist[256];
+    __shared__ int scratch[4];
+    __shared__ int last;
+    pdl_launch();
+    pdl_wait();
+    const uint16_t* lg = p.logits + (size_t)row * p.ld;
+    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+        keys[i] = (uint16_t)key_of_bf16(lg[lo + i]);
+        idx[i] = (uint32_t)(p.base + lo + i);
+    }
+    __syncthreads();
+    uint32_t* mine = p.cand + ((size_t)row * p.nblk + blk) * 2 * kTopK;
+    block_top32(keys, idx, cnt, mine, mine + kTopK, hist, scratch);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(p.ticket + row, 1) == p.nblk - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // merge: the candidates of every block, in block order (indices ascend with block, then rank in list)
+    const uint32_t* all = p.cand + (size_t)row * p.nblk * 2 * kTopK;
+    int m = 0;
+    // keep only real entries; lay them out in ascending index order per block (lists are key-sorted: re-sort
+    // by index is unnecessary because equal keys inside one list are already in index order and blocks ascend)
+    for (int i = threadIdx.x; i < p.nblk * kTopK; i += blockDim.x) {
+        const int bb = i / kTopK, j = i % kTopK;
+        keys[i] = (uint16_t)__ldcg(all + (size_t)bb * 2 * kTopK + j);
+        idx[i] = __ldcg(all + (size_t)bb * 2 * kTopK + kTopK + j);
+    }
+    __syncthreads();
+    m = p.nblk * kTopK;
+    // entries with key 0 are empty fillers (index 0xffffffff): a real bf16 logit never has key 0 except -NaN
+    __shared__ uint32_t ok_[kTopK], oi_[kTopK];
+    block_top32(keys, idx, m, ok_, oi_, hist, scratch);
+    if (threadIdx.x < kTopK) {
+        p.lists[(size_t)row * 2 * kTopK + threadIdx.x] = ok_[threadIdx.x];
+        p.lists[(size_t)row * 2 * kTopK + kTopK + threadIdx.x] = oi_[threadIdx.x];
+    }
+    if (threadIdx.x == 0) {
+        if (p.argmax) p.argmax[row] = (int32_t)oi_[0];
+        p.ticket[row] = 0;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ rows in / feed
+__global__ void embed_rows_kernel(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x,
+                                  int rows, uint32_t* err) {
+    const int b = blockIdx.x;
+    pdl_launch();
+    pdl_wait();
+    const int t = tok->token[b];
+    if (t >= 0 && (embed == nullptr || t >= vocab)) {
+        if (threadIdx.x == 0) atomicOr(err, kErrBounds);
+        return;
+    }
+    for (int i = threadIdx.x; i < kHidden / 8; i += blockDim.x) {
+        float4* dst = reinterpret_cast<float4*>(x + (size_t)b * kHidden) + 2 * i;
+        if (t >= 0) {
+            const uint4 e = reinterpret_cast<const uint4*>(embed + (size_t)t * kHidden)[i];
+            dst[0] = make_float4(bf16lo(e.x), bf16hi(e.x), bf16lo(e.y), bf16hi(e.y));
+            dst[1] = make_float4(bf16lo(e.z), bf16hi(e.z), bf16lo(e.w), bf16hi(e.w));
+        } else {
+            const float4* s = reinterpret_cast<const float4*>(x0 + (size_t)b * kHidden) + 2 * i;
+            dst[0] = s[0];
+            dst[1] = s[1];
+        }
+    }
+}
+
+__global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows) {
+    pdl_launch();
+    pdl_wait();
+    const int b = threadIdx.x;
+    if (b < rows) {
+        const int a = argmax ? argmax[b] : -1;
+        const int np = tok->pos[b] + 1;
+        if (out) {
+            out[b * 4 + 0] = a;
+            out[b * 4 + 1] = np;
+        }
+        if (tok->feed && argmax) {
+            tok->token[b] = a;
+            tok->pos[b] = np;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) tok->step += 1;
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cudaLaunchAttribute* at, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = g;
+    cfg.blockDim = b;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st) {
+    const int rows_pad = (rows + 3) & ~3;
+    const size_t total16 = (size_t)rows_pad * K / 16;
+    tile_weight_kernel<<<1024, 256, 0, st>>>(src, rows, K, dst, total16);
+    return cudaGetLastError();
+}
+
+cudaError_t quantize_fp8_launch(const float* w, int N, int K, uint8_t* q, float* scales, cudaStream_t st) {
+    dim3 grid((K + 127) / 128, (N + 127) / 128);
+    quantize_fp8_kernel<<<grid, 256, 0, st>>>(w, N, K, q, scales);
+    return cudaGetLastError();
+}
+
+int topk_default_blocks(int n) {
+    int nb = (n + 2047) / 2048;
+    return nb < 1 ? 1 : (nb > 128 ? 128 : nb);
+}
+
+size_t topk_workspace_bytes(int rows, int nblk) {
+    return (size_t)rows * nblk * 2 * kTopK * 4 + 256 + (size_t)rows * 4;
+}
+
+cudaError_t topk_launch(int rows, const uint16_t* logits, int n, int ld, int base, uint32_t* lists, int32_t* argmax,
+                        void* work, int nblk, cudaStream_t st, bool pdl) {
+    TopkParams p;
+    p.logits = logits;
+    p.n = n;
+    p.ld = ld;
+    p.base = base;
+    p.rows = rows;
+    p.nblk = nblk;
+    p.cand = static_cast<uint32_t*>(work);
+    p.ticket = reinterpret_cast<int*>(static_cast<uint8_t*>(work) + (size_t)rows * nblk * 2 * kTopK * 4 + 256);
+    p.lists = lists;
+    p.argmax = argmax;
+    const int per = (n + nblk - 1) / nblk;
+    const int cap = per > nblk * kTopK ? per : nblk * kTopK;
+    const size_t smem = ((size_t)cap * 2 + 15) / 16 * 16 + (size_t)cap * 4;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(nblk, rows), dim3(kTopkThreads), smem, st, at, pdl);
+    return cudaLaunchKernelEx(&cfg, topk_kernel, p);
+}
+
+cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x, int rows,
+                              uint32_t* err, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(320), 0, st, at, pdl);
+    return cudaLaunchKernelEx(&cfg, embed_rows_kernel, tok, x0, embed, vocab, x, rows, err);
+}
+
+cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl) {
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(32), 0, st, at, pdl);
+    return cudaLaunchKernelEx(&cfg, feed_kernel, tok, argmax, out, rows);
+}
+
+}  // namespace qres
+
+namespace qres {
+
+// merge nlists per-rank lists ([nlists][rows][64], keys then indices, ranks in vocab order) into one list per
+// row and its argmax (the hubs' exchange + merge, mlp_hub.cpp:366-411 / sampling.hpp merge)
+__global__ void __launch_bounds__(256) merge_lists_kernel(const uint32_t* lists, int nlists, int rows, uint32_t* out,
+                                                          int32_t* argmax) {
+    const int row = blockIdx.x;
+    __shared__ uint16_t keys[8 * kTopK];
+    __shared__ uint32_t idx[8 * kTopK];
+    __shared__ int hist[256];
+    __shared__ int scratch[4];
+    __shared__ uint32_t ok_[kTopK], oi_[kTopK];
+    pdl_launch();
+    pdl_wait();
+    const int n = nlists * kTopK;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int l = i / kTopK, j = i % kTopK;
+        const uint32_t* src = lists + ((size_t)l * rows + row) * 2 * kTopK;
+        keys[i] = (uint16_t)src[j];
+        idx[i] = src[kTopK + j];
+    }
+    __syncthreads();
+    block_top32(keys, idx, n, ok_, oi_, hist, scratch);
+    if (threadIdx.x < kTopK) {
+        out[(size_t)row * 2 * kTopK + threadIdx.x] = ok_[threadIdx.x];
+        out[(size_t)row * 2 * kTopK + kTopK + threadIdx.x] = oi_[threadIdx.x];
+    }
+    if (threadIdx.x == 0 && argmax) argmax[row] = (int32_t)oi_[0];
+}
+
+cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint32_t* out, int32_t* argmax,
+                               cudaStream_t st, bool pdl) {
+    if (nlists < 1 || nlists > 8) return cudaErrorInvalidValue;
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(256), 0, st, at, pdl);
+    return cudaLaunchKernelEx(&cfg, merge_lists_kernel, lists, nlists, rows, out, argmax);
+}
+
+}  // namespace qres

@@ -1,0 +1,641 @@
+// libqres C ABI: context, buffer binding, the decode step as a sequence of programmatic-dependent launches,
+// its CUDA-graph capture, NCCL for tensor parallelism, and the single-kernel entry points.
+//
+// The step (ResidentModel.step, qwen36_resident/model.py:1499-1508, one launch of the per-chip program) is,
+// per rank:
+//   rows in (x0 or embed[token])
+//   per layer: in-proj GEMV (rmsnorm prologue)  -> GDN or attention mixer -> out-proj GEMV (+ residual)
+//              gate|up GEMV (rmsnorm prologue, SwiGLU epilogue) -> down GEMV (+ residual)
+//   lm_head GEMV -> top-32 / argmax (-> cross-rank merge) -> next-token feed
+// With nranks > 1 the out / down GEMVs write fp32 partials, NCCL all-reduces them, and the next GEMV's
+// prologue adds them to the residual (x_out = x + sum of partials), alternating two residual buffers.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "qres_common.cuh"
+
+namespace qres {
+cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int epi, void* out, int ld_out,
+                        int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out);
+cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
+                       const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
+                       uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl);
+size_t attn_workspace_bytes(int nranks, int rows, int nchunks);
+int attn_default_chunks(int nranks, int rows, int sm_count, int max_pages);
+cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const int32_t* page_table,
+                        int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
+                        const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
+                        void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl);
+cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st);
+cudaError_t quantize_fp8_launch(const float* w, int N, int K, uint8_t* q, float* scales, cudaStream_t st);
+int topk_default_blocks(int n);
+size_t topk_workspace_bytes(int rows, int nblk);
+cudaError_t topk_launch(int rows, const uint16_t* logits, int n, int ld, int base, uint32_t* lists, int32_t* argmax,
+                        void* work, int nblk, cudaStream_t st, bool pdl);
+cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint32_t* out, int32_t* argmax,
+                               cudaStream_t st, bool pdl);
+cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x, int rows,
+                              uint32_t* err, cudaStream_t st, bool pdl);
+cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl);
+}  // namespace qres
+
+using namespace qres;
+
+namespace {
+
+std::mutex g_err_mu;
+std::string g_err;  // errors without a context
+
+// NCCL entry points, resolved at run time from the libnccl.so.2 the process uses
+struct Nccl {
+    void* h = nullptr;
+    ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    const char* (*errStr)(ncclResult_t) = nullptr;
+};
+Nccl g_nccl;
+std::mutex g_nccl_mu;
+
+bool load_nccl(const char* libpath, std::string* why) {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.h) return true;
+    void* h = nullptr;
+    if (libpath && *libpath) h = dlopen(libpath, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        *why = std::string("cannot load libnccl.so.2: ") + dlerror();
+        return false;
+    }
+    g_nccl.h = h;
+    g_nccl.getUniqueId = (decltype(g_nccl.getUniqueId))dlsym(h, "ncclGetUniqueId");
+    g_nccl.commInitRank = (decltype(g_nccl.commInitRank))dlsym(h, "ncclCommInitRank");
+    g_nccl.allReduce = (decltype(g_nccl.allReduce))dlsym(h, "ncclAllReduce");
+    g_nccl.allGather = (decltype(g_nccl.allGather))dlsym(h, "ncclAllGather");
+    g_nccl.commDestroy = (decltype(g_nccl.commDestroy))dlsym(h, "ncclCommDestroy");
+    g_nccl.errStr = (decltype(g_nccl.errStr))dlsym(h, "ncclGetErrorString");
+    if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allReduce || !g_nccl.allGather || !g_nccl.commDestroy) {
+        *why = "libnccl.so.2 lacks an entry point";
+        g_nccl.h = nullptr;
+        return false;
+    }
+    return true;
+}
+
+struct Layer {
+    qres_weight w[5] = {};
+    bool has[5] = {false, false, false, false, false};
+    const uint16_t* taps = nullptr;
+    const float *dt = nullptr, *neg_a = nullptr, *norm_w = nullptr;
+    const float *wq = nullptr, *wk = nullptr;
+    qres_layer_state st = {};
+    bool has_st = false;
+};
+
+}  // namespace
+
+struct qres_ctx {
+    qres_config cfg;
+    int rank = 0, nranks = 1, device = 0, sm_count = 148;
+    // per-rank dims
+    int nk = 16, nv = 48, h = 24, nkv = 4, ic = 17408, vocab_local = 0, ld_y = 0, gv = 6144;
+    std::vector<Layer> layers;
+    qres_weight head = {};
+    bool has_head = false;
+    const float *cos_tab = nullptr, *sin_tab = nullptr;
+    int max_pos = 0;
+    qres_io io = {};
+    bool has_io = false;
+    // workspace carve
+    uint8_t* ws = nullptr;
+    size_t ws_bytes = 0;
+    uint32_t* err = nullptr;
+    float *xb = nullptr, *partial = nullptr;
+    uint16_t *y = nullptr, *o = nullptr, *a = nullptr;
+    int32_t* argmax = nullptr;
+    uint32_t* gathered = nullptr;
+    void* attn_work = nullptr;
+    size_t attn_work_bytes = 0;
+    int attn_chunks = 1;
+    void* topk_work = nullptr;
+    int topk_blk = 1;
+    ncclComm_t comm = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+    std::string last_error;
+};
+
+namespace {
+
+qres_status fail(qres_ctx* c, qres_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (c) {
+        c->last_error = buf;
+    } else {
+        std::lock_guard<std::mutex> lk(g_err_mu);
+        g_err = buf;
+    }
+    return s;
+}
+
+#define CU(ctx, call)                                                                                      \
+    do {                                                                                                   \
+        cudaError_t e_ = (call);                                                                           \
+        if (e_ != cudaSuccess) return fail(ctx, QRES_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                            \
+    } while (0)
+
+bool is_attn(const qres_ctx* c, int l) {
+    return c->cfg.attn_interval > 0 && (l + 1) % c->cfg.attn_interval == 0;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// workspace layout: offsets of each scratch region
+struct Carve {
+    size_t err, xb, partial, y, o, a, argmax, gathered, attn, topk, total;
+};
+
+Carve carve(const qres_ctx* c) {
+    Carve k;
+    const int R = c->cfg.rows;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = off;
+        off = align256(off + bytes);
+        return at;
+    };
+    k.err = take(256);
+    k.xb = take((size_t)R * kHidden * 4);
+    k.partial = take((size_t)R * kHidden * 4);
+    k.y = take((size_t)R * c->ld_y * 2);
+    k.o = take((size_t)R * c->gv * 2);
+    k.a = take((size_t)R * c->ic * 2);
+    k.argmax = take((size_t)R * 4);
+    k.gathered = take((size_t)c->nranks * R * 2 * QRES_TOPK * 4);
+    k.attn = take(attn_workspace_bytes(c->nranks, R, c->attn_chunks));
+    k.topk = take(c->vocab_local ? topk_workspace_bytes(R, c->topk_blk) : 0);
+    k.total = off;
+    return k;
+}
+
+qres_status check_weight(qres_ctx* c, const qres_weight* w, int rows, int K, const char* what) {
+    if (!w || !w->data || !w->scales || !w->sidx) return fail(c, QRES_ERR_ARG, "%s: null pointer", what);
+    if (w->rows != rows || w->K != K || w->rows_pad != ((rows + 3) & ~3) || w->n_scale_rows < 1)
+        return fail(c, QRES_ERR_ARG, "%s: shape rows=%d K=%d rows_pad=%d (want rows=%d K=%d)", what, w->rows, w->K,
+                    w->rows_pad, rows, K);
+    return QRES_OK;
+}
+
+}  // namespace
+
+// =============================================================================================== C ABI
+extern "C" {
+
+qres_status qres_last_error(const qres_ctx* ctx, char* buf, size_t len) {
+    if (!buf || !len) return QRES_ERR_ARG;
+    std::string s;
+    if (ctx) {
+        s = ctx->last_error;
+    } else {
+        std::lock_guard<std::mutex> lk(g_err_mu);
+        s = g_err;
+    }
+    snprintf(buf, len, "%s", s.c_str());
+    return QRES_OK;
+}
+
+qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qres_ctx** out) {
+    if (!cfg || !out) return fail(nullptr, QRES_ERR_ARG, "qres_create: null argument");
+    if (!(nranks == 1 || nranks == 2 || nranks == 4 || nranks == 8) || rank < 0 || rank >= nranks)
+        return fail(nullptr, QRES_ERR_ARG, "qres_create: rank %d of %d (nranks must be 1, 2, 4 or 8)", rank, nranks);
+    if (cfg->rows < 1 || cfg->rows > QRES_MAX_ROWS || cfg->layers < 1)
+        return fail(nullptr, QRES_ERR_ARG, "qres_create: rows %d, layers %d", cfg->rows, cfg->layers);
+    if (cfg->vocab % nranks) return fail(nullptr, QRES_ERR_ARG, "qres_create: vocab %d not divisible by %d", cfg->vocab, nranks);
+    qres_ctx* c = new qres_ctx();
+    c->cfg = *cfg;
+    c->rank = rank;
+    c->nranks = nranks;
+    cudaGetDevice(&c->device);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
+    c->sm_count = cfg->sm_count > 0 ? cfg->sm_count : sms;
+    c->nk = 16 / nranks;
+    c->nv = 48 / nranks;
+    c->h = 24 / nranks;
+    c->nkv = nranks <= 4 ? 4 / nranks : 1;
+    c->ic = 17408 / nranks;
+    c->gv = 6144 / nranks;
+    c->vocab_local = cfg->vocab / nranks;
+    const int n_gdn = 2 * c->nk * kDK + 2 * c->nv * kDV + 2 * c->nv;
+    const int n_attn = 2 * c->h * kHD + 2 * c->nkv * kHD;
+    c->ld_y = ((n_gdn > n_attn ? n_gdn : n_attn) + 7) & ~7;
+    c->layers.resize(cfg->layers);
+    c->attn_chunks = attn_default_chunks(nranks, cfg->rows, c->sm_count, cfg->max_pages > 0 ? cfg->max_pages : 1);
+    c->topk_blk = c->vocab_local ? topk_default_blocks(c->vocab_local) : 1;
+    *out = c;
+    return QRES_OK;
+}
+
+qres_status qres_destroy(qres_ctx* ctx) {
+    if (!ctx) return QRES_OK;
+    if (ctx->exec) cudaGraphExecDestroy(ctx->exec);
+    if (ctx->graph) cudaGraphDestroy(ctx->graph);
+    if (ctx->comm && g_nccl.commDestroy) g_nccl.commDestroy(ctx->comm);
+    delete ctx;
+    return QRES_OK;
+}
+
+qres_status qres_load_weights(qres_ctx* c, int32_t layer, int32_t kind, const qres_weight* w) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    if (kind == QRES_W_HEAD) {
+        if (!c->vocab_local) return fail(c, QRES_ERR_ARG, "lm_head bound but vocab is 0");
+        qres_status s = check_weight(c, w, c->vocab_local, kHidden, "lm_head");
+        if (s) return s;
+        c->head = *w;
+        c->has_head = true;
+        return QRES_OK;
+    }
+    if (layer < 0 || layer >= c->cfg.layers || kind < 0 || kind > QRES_W_DOWN)
+        return fail(c, QRES_ERR_ARG, "qres_load_weights: layer %d kind %d", layer, kind);
+    int rows = 0, K = kHidden;
+    switch (kind) {
+        case QRES_W_GDN_IN: rows = 2 * c->nk * kDK + 2 * c->nv * kDV + 2 * c->nv; break;
+        case QRES_W_ATTN_IN: rows = 2 * c->h * kHD + 2 * c->nkv * kHD; break;
+        case QRES_W_OUT: rows = kHidden; K = c->gv; break;
+        case QRES_W_GATEUP: rows = 2 * c->ic; break;
+        case QRES_W_DOWN: rows = kHidden; K = c->ic; break;
+    }
+    if (kind == QRES_W_GDN_IN && is_attn(c, layer)) return fail(c, QRES_ERR_ARG, "layer %d is attention", layer);
+    if (kind == QRES_W_ATTN_IN && !is_attn(c, layer)) return fail(c, QRES_ERR_ARG, "layer %d is GDN", layer);
+    qres_status s = check_weight(c, w, rows, K, "projection");
+    if (s) return s;
+    c->layers[layer].w[kind] = *w;
+    c->layers[layer].has[kind] = true;
+    return QRES_OK;
+}
+
+qres_status qres_load_gdn_params(qres_ctx* c, int32_t layer, const uint16_t* taps, const float* dt, const float* neg_a,
+                                 const float* norm_w) {
+    if (!c || layer < 0 || layer >= c->cfg.layers || !taps || !dt || !neg_a || !norm_w)
+        return fail(c, QRES_ERR_ARG, "qres_load_gdn_params: bad argument");
+    Layer& L = c->layers[layer];
+    L.taps = taps;
+    L.dt = dt;
+    L.neg_a = neg_a;
+    L.norm_w = norm_w;
+    return QRES_OK;
+}
+
+qres_status qres_load_attn_params(qres_ctx* c, int32_t layer, const float* wq, const float* wk) {
+    if (!c || layer < 0 || layer >= c->cfg.layers || !wq || !wk)
+        return fail(c, QRES_ERR_ARG, "qres_load_attn_params: bad argument");
+    c->layers[layer].wq = wq;
+    c->layers[layer].wk = wk;
+    return QRES_OK;
+}
+
+qres_status qres_bind_state(qres_ctx* c, int32_t layer, const qres_layer_state* st) {
+    if (!c || !st || layer < 0 || layer >= c->cfg.layers) return fail(c, QRES_ERR_ARG, "qres_bind_state: bad argument");
+    if (is_attn(c, layer) ? (!st->k_pool || !st->v_pool) : (!st->gdn_state || !st->conv_hist))
+        return fail(c, QRES_ERR_ARG, "qres_bind_state: layer %d lacks its buffers", layer);
+    c->layers[layer].st = *st;
+    c->layers[layer].has_st = true;
+    return QRES_OK;
+}
+
+qres_status qres_bind_rope(qres_ctx* c, const float* cos_tab, const float* sin_tab, int32_t max_pos) {
+    if (!c || !cos_tab || !sin_tab || max_pos < 1) return fail(c, QRES_ERR_ARG, "qres_bind_rope: bad argument");
+    c->cos_tab = cos_tab;
+    c->sin_tab = sin_tab;
+    c->max_pos = max_pos;
+    return QRES_OK;
+}
+
+qres_status qres_bind_io(qres_ctx* c, const qres_io* io) {
+    if (!c || !io || !io->tok || !io->x) return fail(c, QRES_ERR_ARG, "qres_bind_io: tok and x are required");
+    if (c->vocab_local && (!io->logits || !io->topk || !io->out))
+        return fail(c, QRES_ERR_ARG, "qres_bind_io: the lm_head needs logits, topk and out");
+    c->io = *io;
+    c->has_io = true;
+    return QRES_OK;
+}
+
+qres_status qres_workspace_size(const qres_ctx* c, size_t* bytes) {
+    if (!c || !bytes) return QRES_ERR_ARG;
+    *bytes = carve(c).total;
+    return QRES_OK;
+}
+
+qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
+    if (!c || !dev) return fail(c, QRES_ERR_ARG, "qres_bind_workspace: null");
+    Carve k = carve(c);
+    if (bytes < k.total) return fail(c, QRES_ERR_ARG, "qres_bind_workspace: %zu bytes, need %zu", bytes, k.total);
+    uint8_t* w = static_cast<uint8_t*>(dev);
+    CU(c, cudaMemset(w, 0, k.total));
+    CU(c, cudaDeviceSynchronize());
+    c->ws = w;
+    c->ws_bytes = bytes;
+    c->err = reinterpret_cast<uint32_t*>(w + k.err);
+    c->xb = reinterpret_cast<float*>(w + k.xb);
+    c->partial = reinterpret_cast<float*>(w + k.partial);
+    c->y = reinterpret_cast<uint16_t*>(w + k.y);
+    c->o = reinterpret_cast<uint16_t*>(w + k.o);
+    c->a = reinterpret_cast<uint16_t*>(w + k.a);
+    c->argmax = reinterpret_cast<int32_t*>(w + k.argmax);
+    c->gathered = reinterpret_cast<uint32_t*>(w + k.gathered);
+    c->attn_work = w + k.attn;
+    c->attn_work_bytes = attn_workspace_bytes(c->nranks, c->cfg.rows, c->attn_chunks);
+    c->topk_work = c->vocab_local ? (void*)(w + k.topk) : nullptr;
+    return QRES_OK;
+}
+
+qres_status qres_nccl_unique_id(const char* libpath, void* id128) {
+    std::string why;
+    if (!id128) return fail(nullptr, QRES_ERR_ARG, "null id");
+    if (!load_nccl(libpath, &why)) return fail(nullptr, QRES_ERR_COMM, "%s", why.c_str());
+    ncclUniqueId id;
+    ncclResult_t r = g_nccl.getUniqueId(&id);
+    if (r != ncclSuccess) return fail(nullptr, QRES_ERR_COMM, "ncclGetUniqueId: %d", (int)r);
+    memcpy(id128, &id, sizeof id);
+    return QRES_OK;
+}
+
+qres_status qres_nccl_init(qres_ctx* c, const char* libpath, const void* id128) {
+    std::string why;
+    if (!c || !id128) return fail(c, QRES_ERR_ARG, "null argument");
+    if (!load_nccl(libpath, &why)) return fail(c, QRES_ERR_COMM, "%s", why.c_str());
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof id);
+    ncclResult_t r = g_nccl.commInitRank(&c->comm, c->nranks, id, c->rank);
+    if (r != ncclSuccess)
+        return fail(c, QRES_ERR_COMM, "ncclCommInitRank: %s", g_nccl.errStr ? g_nccl.errStr(r) : "error");
+    return QRES_OK;
+}
+
+static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
+    const int R = c->cfg.rows, n = c->nranks;
+    const bool tp = n > 1;
+    if (!c->has_io || !c->ws) return fail(c, QRES_ERR_STATE, "decode step before bind_io / bind_workspace");
+    if (tp && !c->comm) return fail(c, QRES_ERR_STATE, "nranks > 1 needs qres_nccl_init");
+    if (c->cfg.vocab && !c->has_head) return fail(c, QRES_ERR_STATE, "lm_head not loaded");
+    for (int l = 0; l < c->cfg.layers; ++l) {
+        const Layer& L = c->layers[l];
+        const bool at = is_attn(c, l);
+        if (!L.has[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN] || !L.has[QRES_W_OUT] || !L.has[QRES_W_GATEUP] ||
+            !L.has[QRES_W_DOWN] || !L.has_st)
+            return fail(c, QRES_ERR_STATE, "layer %d: weights or state not bound", l);
+        if (at ? (!L.wq || !c->cos_tab || !c->io.page_table) : (!L.taps))
+            return fail(c, QRES_ERR_STATE, "layer %d: parameters not bound", l);
+    }
+    const int grid = c->sm_count;
+    const int32_t* pos = c->io.tok->pos;
+    int launches = 0;
+    auto K = [&](cudaError_t e, const char* what) -> qres_status {
+        if (e != cudaSuccess) return fail(c, QRES_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+        ++launches;
+        return QRES_OK;
+    };
+#define STEP(call, what)                       \
+    do {                                       \
+        qres_status s_ = K((call), what);      \
+        if (s_) return s_;                     \
+    } while (0)
+    float* cur = c->io.x;  // residual stream
+    float* other = c->xb;
+    STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
+    bool pending = false;  // all-reduced partials waiting to be added to cur
+    auto allreduce = [&]() -> qres_status {
+        ncclResult_t r = g_nccl.allReduce(c->partial, c->partial, (size_t)R * kHidden, ncclFloat32, ncclSum, c->comm, st);
+        if (r != ncclSuccess) return fail(c, QRES_ERR_COMM, "ncclAllReduce: %d", (int)r);
+        return QRES_OK;
+    };
+    // a GEMV with the rmsnorm prologue over the residual (adding pending partials first when TP)
+    auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
+        if (pending) {
+            qres_status s = K(gemv_launch(w, R, 2, cur, epi, out, ld_out, grid, c->err, st, true, c->partial, other), what);
+            std::swap(cur, other);
+            pending = false;
+            return s;
+        }
+        return K(gemv_launch(w, R, 0, cur, epi, out, ld_out, grid, c->err, st, true, nullptr, nullptr), what);
+    };
+    auto row_parallel = [&](const qres_weight& w, const uint16_t* in, const char* what) -> qres_status {
+        if (!tp) return K(gemv_launch(w, R, 1, in, 2, cur, kHidden, grid, c->err, st, true, nullptr, nullptr), what);
+        qres_status s = K(gemv_launch(w, R, 1, in, 3, c->partial, kHidden, grid, c->err, st, true, nullptr, nullptr), what);
+        if (s) return s;
+        s = allreduce();
+        pending = true;
+        return s;
+    };
+    for (int l = 0; l < c->cfg.layers; ++l) {
+        const Layer& L = c->layers[l];
+        const bool at = is_attn(c, l);
+        uint16_t* mcopy = (l == c->cfg.layers - 1) ? c->io.mixer_out : nullptr;
+        qres_status s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
+        if (s) return s;
+        if (at) {
+            STEP(attn_launch(n, R, c->y, c->ld_y, pos, c->io.page_table, c->cfg.max_pages, c->cfg.num_pages, L.wq, L.wk,
+                             c->cos_tab, c->sin_tab, c->max_pos, L.st.k_pool, L.st.v_pool, c->o, mcopy, c->attn_work,
+                             c->attn_work_bytes, c->attn_chunks, c->err, st, true),
+                 "attention");
+        } else {
+            STEP(gdn_launch(n, R, c->y, c->ld_y, pos, L.taps, L.dt, L.neg_a, L.norm_w, L.st.gdn_state, L.st.conv_hist,
+                            c->o, mcopy, c->err, st, true),
+                 "gdn");
+        }
+        s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");
+        if (s) return s;
+        s = norm_gemv(L.w[QRES_W_GATEUP], 1, c->a, c->ic, "gate-up");
+        if (s) return s;
+        s = row_parallel(L.w[QRES_W_DOWN], c->a, "down");
+        if (s) return s;
+    }
+    if (c->cfg.vocab) {
+        qres_status s = norm_gemv(c->head, 0, c->io.logits, c->vocab_local, "lm_head");
+        if (s) return s;
+        const int base = c->rank * c->vocab_local;
+        if (!tp) {
+            STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, c->argmax, c->topk_work,
+                             c->topk_blk, st, true),
+                 "top-k");
+        } else {
+            STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, nullptr, c->topk_work,
+                             c->topk_blk, st, true),
+                 "top-k");
+            ncclResult_t r = g_nccl.allGather(c->io.topk, c->gathered, (size_t)R * 2 * QRES_TOPK, ncclUint32, c->comm, st);
+            if (r != ncclSuccess) return fail(c, QRES_ERR_COMM, "ncclAllGather: %d", (int)r);
+            STEP(merge_lists_launch(c->gathered, n, R, c->io.topk, c->argmax, st, true), "merge");
+        }
+        STEP(feed_launch(c->io.tok, c->argmax, c->io.out, R, st, true), "feed");
+    } else {
+        STEP(feed_launch(c->io.tok, nullptr, nullptr, R, st, true), "feed");
+    }
+    if (cur != c->io.x) CU(c, cudaMemcpyAsync(c->io.x, cur, (size_t)R * kHidden * 4, cudaMemcpyDeviceToDevice, st));
+#undef STEP
+    c->launches = launches;
+    return QRES_OK;
+}
+
+qres_status qres_decode_step(qres_ctx* c, void* stream) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    if (c->nranks > 1 && !c->cfg.vocab)
+        return fail(c, QRES_ERR_ARG, "nranks > 1 without an lm_head is not supported");
+    return enqueue_step(c, static_cast<cudaStream_t>(stream));
+}
+
+qres_status qres_capture(qres_ctx* c, void* stream) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    qres_release_graph(c);
+    CU(c, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    qres_status s = qres_decode_step(c, stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (s) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+    }
+    if (e != cudaSuccess) return fail(c, QRES_ERR_CUDA, "end capture: %s", cudaGetErrorString(e));
+    c->graph = g;
+    CU(c, cudaGraphInstantiate(&c->exec, g, 0));
+    return QRES_OK;
+}
+
+qres_status qres_replay(qres_ctx* c, void* stream) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    if (!c->exec) return fail(c, QRES_ERR_STATE, "replay without a captured graph");
+    CU(c, cudaGraphLaunch(c->exec, static_cast<cudaStream_t>(stream)));
+    return QRES_OK;
+}
+
+qres_status qres_release_graph(qres_ctx* c) {
+    if (!c) return QRES_ERR_ARG;
+    if (c->exec) cudaGraphExecDestroy(c->exec);
+    if (c->graph) cudaGraphDestroy(c->graph);
+    c->exec = nullptr;
+    c->graph = nullptr;
+    return QRES_OK;
+}
+
+qres_status qres_check(qres_ctx* c, void* stream) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    CU(c, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    if (!c->err) return QRES_OK;
+    uint32_t w = 0;
+    CU(c, cudaMemcpy(&w, c->err, 4, cudaMemcpyDeviceToHost));
+    if (!w) return QRES_OK;
+    CU(c, cudaMemset(c->err, 0, 4));
+    return fail(c, QRES_ERR_DEVICE, "device error word 0x%x:%s%s%s", w, (w & kErrTimeout) ? " bounded wait ran out;" : "",
+                (w & kErrBounds) ? " index out of range (position / page / token);" : "",
+                (w & kErrPeer) ? " peer epoch mismatch;" : "");
+}
+
+int32_t qres_step_launches(const qres_ctx* c) { return c ? c->launches : 0; }
+
+// ---- single kernels ----
+
+qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
+                      int32_t grid, uint32_t* err, void* stream) {
+    if (!w || !in || !out || pro < 0 || pro > 1 || epi < 0 || epi > 3)
+        return fail(nullptr, QRES_ERR_ARG, "qres_gemv: bad argument");
+    int sms = 148;
+    if (grid <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        grid = sms;
+    }
+    const int ld_out = epi == 1 ? w->rows / 2 : w->rows;
+    cudaError_t e = gemv_launch(*w, rows, pro, in, epi, out, ld_out, grid, err, static_cast<cudaStream_t>(stream), false,
+                                nullptr, nullptr);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_gdn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int32_t ld_y, const int32_t* pos,
+                           const uint16_t* taps, const float* dt, const float* neg_a, const float* norm_w, float* state,
+                           uint16_t* conv_hist, uint16_t* o, uint32_t* err, void* stream) {
+    if (!y || !pos || !taps || !dt || !neg_a || !norm_w || !state || !conv_hist || !o)
+        return fail(nullptr, QRES_ERR_ARG, "qres_gdn_mixer: null argument");
+    cudaError_t e = gdn_launch(nranks, rows, y, ld_y, pos, taps, dt, neg_a, norm_w, state, conv_hist, o, nullptr, err,
+                               static_cast<cudaStream_t>(stream), false);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gdn_mixer: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_attn_workspace_size(int32_t nranks, int32_t rows, int32_t max_pos, size_t* bytes) {
+    if (!bytes || nranks < 1 || rows < 1) return fail(nullptr, QRES_ERR_ARG, "qres_attn_workspace_size: bad argument");
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int pages = (max_pos + kKvBlock - 1) / kKvBlock;
+    *bytes = attn_workspace_bytes(nranks, rows, attn_default_chunks(nranks, rows, sms, pages));
+    return QRES_OK;
+}
+
+qres_status qres_attn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int32_t ld_y, const int32_t* pos,
+                            const int32_t* page_table, int32_t max_pages, const float* wq, const float* wk,
+                            const float* cos_tab, const float* sin_tab, uint16_t* k_pool, uint16_t* v_pool, uint16_t* o,
+                            void* work, size_t work_bytes, uint32_t* err, void* stream) {
+    if (!y || !pos || !page_table || !wq || !wk || !cos_tab || !sin_tab || !k_pool || !v_pool || !o || !work)
+        return fail(nullptr, QRES_ERR_ARG, "qres_attn_mixer: null argument");
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int chunks = attn_default_chunks(nranks, rows, sms, max_pages);
+    // num_pages / max_pos bounds: the caller's pool holds max_pages * rows pages at most in this entry point
+    cudaError_t e = attn_launch(nranks, rows, y, ld_y, pos, page_table, max_pages, max_pages * rows, wq, wk, cos_tab,
+                                sin_tab, max_pages * kKvBlock, k_pool, v_pool, o, nullptr, work, work_bytes, chunks, err,
+                                static_cast<cudaStream_t>(stream), false);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_attn_mixer: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_topk_workspace_size(int32_t rows, int32_t n_logits, size_t* bytes) {
+    if (!bytes || rows < 1 || n_logits < 1) return QRES_ERR_ARG;
+    *bytes = topk_workspace_bytes(rows, topk_default_blocks(n_logits));
+    return QRES_OK;
+}
+
+qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base, uint32_t* lists,
+                      int32_t* argmax, void* work, size_t work_bytes, void* stream) {
+    if (!logits || !lists || !work || rows < 1 || n_logits < 1) return fail(nullptr, QRES_ERR_ARG, "qres_topk: bad argument");
+    const int nblk = topk_default_blocks(n_logits);
+    if (work_bytes < topk_workspace_bytes(rows, nblk)) return fail(nullptr, QRES_ERR_ARG, "qres_topk: workspace too small");
+    cudaError_t e = topk_launch(rows, logits, n_logits, n_logits, base, lists, argmax, work, nblk,
+                                static_cast<cudaStream_t>(stream), false);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_topk: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_quantize_fp8(const float* w, int32_t N, int32_t K, uint8_t* q, float* scales, void* stream) {
+    if (!w || !q || !scales || N < 1 || K < 1) return fail(nullptr, QRES_ERR_ARG, "qres_quantize_fp8: bad argument");
+    cudaError_t e = quantize_fp8_launch(w, N, K, q, scales, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_quantize_fp8: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_tile_weight(const uint8_t* src, int32_t rows, int32_t K, uint8_t* dst, void* stream) {
+    if (!src || !dst || rows < 1 || K % 128) return fail(nullptr, QRES_ERR_ARG, "qres_tile_weight: bad argument");
+    cudaError_t e = tile_weight_launch(src, rows, K, dst, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_tile_weight: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+}  // extern "C"

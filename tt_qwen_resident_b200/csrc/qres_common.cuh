@@ -1,0 +1,153 @@
+// Shared device helpers of libqres: sm_100a PTX wrappers (mbarrier, bulk async copies, programmatic
+// dependent launch), bounded waits that report instead of hanging, and the numeric helpers every kernel of the
+// resident decode step uses.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qres.h"
+
+namespace qres {
+
+constexpr int kHidden = 5120;
+constexpr int kDK = 128, kDV = 128;
+constexpr int kHD = 256, kRot = 64;
+constexpr int kKvBlock = 64;
+constexpr int kMaxRows = 8;  // users (or verify rows) per step
+constexpr float kEps = 1e-6f;
+
+// error bits written into the context's device error word (qres_dev_status)
+enum : uint32_t {
+    kErrTimeout = 1u << 0,   // a bounded wait ran out (mbarrier / peer flag)
+    kErrBounds = 1u << 1,    // an index (position, page, token) outside its table
+    kErrPeer = 1u << 2,      // a peer flag carried an unexpected epoch
+};
+
+// ---- numeric helpers -------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// IEEE-rounded helpers (no FMA contraction) where the reference's torch ops round each product / sum
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+// torch.nn.functional.softplus (beta 1, threshold 20)
+__device__ __forceinline__ float softplus_f(float v) { return v > 20.0f ? v : log1pf(expf(v)); }
+__device__ __forceinline__ float rsqrt_ieee(float v) { return 1.0f / sqrtf(v); }
+
+// 4 e4m3 bytes -> 4 floats (exact), through the packed e4m3x2 -> f16x2 conversion
+__device__ __forceinline__ void fp8x4_to_f32(uint32_t w, float* f) {
+    __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xffffu), __NV_E4M3);
+    __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3);
+    float2 a = __half22float2(*reinterpret_cast<__half2*>(&lo));
+    float2 b = __half22float2(*reinterpret_cast<__half2*>(&hi));
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---- programmatic dependent launch --------------------------------------------------------------------------
+// wait: every prerequisite grid has completed and its memory is visible; launch_dependents: allow the next
+// kernel in the stream to be scheduled (its pre-wait part -- weight prefetch -- overlaps this kernel's tail)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---- mbarrier + bulk async copy (cp.async.bulk, no multicast) ----------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// spin budget of a bounded wait: ~2^22 try_wait rounds (each suspends for a while) -- far beyond any legitimate
+// wait of this code, well short of a hang
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// wait for the phase with the given parity to complete; false (and the error bit set) when the budget runs out
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    if (err) atomicOr(err, kErrTimeout);
+    return false;
+}
+
+// global -> shared bulk copy completing on an mbarrier (sizes and addresses multiples of 16 bytes)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// L2 prefetch of a global range (no shared destination)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// named barrier over a subset of warps (id 1.., count a multiple of 32)
+__device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_addr(p)));
+    return v;
+}
+
+// streaming read-only global load (no L1 allocation)
+__device__ __forceinline__ uint4 ldg_nc128(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace qres

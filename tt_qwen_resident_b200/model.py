@@ -1,0 +1,358 @@
+"""The resident decode model on B200: the host object of sott0n/tt-qwen-resident's ``ResidentModel``
+(qwen36_resident/model.py:403-1598) over libqres.
+
+Same method names and meaning: ``token_state`` builds a step's input (x0 rows or tokens, positions), ``step``
+runs one decode step (asynchronously, on the current stream), ``x`` / ``mixer_output`` / ``logits`` /
+``argmax`` / ``fed_token`` read its results, ``reset`` / ``load_state`` write the decode state,
+``capture_trace`` / ``release_trace`` record / drop the step as a CUDA graph. Weights, state and activations
+live in torch-allocated device memory; every kernel runs in libqres (no torch math on the step's path).
+
+Differences by design: weights are FP8-e4m3 with one fp32 scale per 128x128 block (the reference: Tenstorrent
+bf8/bf4); the KV cache is paged (64 positions per page) in bf16; tensor parallelism is 1, 2, 4 or 8 ranks
+(KV heads replicated on 2 ranks at 8), one process per GPU.
+"""
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from .weights import CONV_CH, DK, DV, HD, HIDDEN, NKV, NV, RankDims, shard, stack_matrices
+
+ROPE_THETA = 10_000_000.0
+ROT = 64
+TOP_K = _lib.QRES_TOPK
+
+
+def is_attn(l, interval):
+    return interval > 0 and (l + 1) % interval == 0
+
+
+def rope_table(max_pos):
+    """cos / sin [max_pos, 32] of model.py:128-131: fp64 angles pos * theta^(-2i/64), rounded to fp32"""
+    inv = 1.0 / ROPE_THETA ** (torch.arange(0, ROT, 2, dtype=torch.float64) / ROT)
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv
+    return torch.cos(ang).float(), torch.sin(ang).float()
+
+
+class ResidentModel:
+    def __init__(
+        self,
+        w,
+        layers,
+        interval,
+        batch=1,
+        max_pos=4096,
+        lm_head=False,
+        embed=None,
+        rank=0,
+        nranks=1,
+        state_copies=None,
+        page_table=None,
+        device="cuda",
+        sm_count=0,
+        nccl_id=None,
+    ):
+        """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
+        kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
+        random_weights copies. state_copies: (gdn, attn) decode states (default one per layer; fewer share a
+        state between layers like the reference's State copies). embed: [vocab, 5120] bf16 table for token
+        rows (device-fed decode). page_table: [batch, max_pages] int32 (default: user b's pages contiguous)."""
+        self.device = torch.device(device)
+        self.layers, self.interval, self.batch = layers, interval, batch
+        self.users = batch
+        self.rank, self.nranks = rank, nranks
+        self.lm_head = lm_head and w.get("head") is not None
+        vocab = w["head"].shape[0] if self.lm_head else 0
+        self.vocab = vocab
+        self.d = d = RankDims(rank, nranks, vocab)
+        self.max_pos = max_pos
+        self.max_pages = -(-max_pos // _lib.QRES_KV_BLOCK)
+        self.n_attn = sum(is_attn(l, interval) for l in range(layers))
+        self.n_gdn = layers - self.n_attn
+        gc, ac = state_copies or (self.n_gdn, self.n_attn)
+        self.state_copies = (max(gc, 1) if self.n_gdn else 0, max(ac, 1) if self.n_attn else 0)
+        L = _lib.lib()
+        cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count, 0)
+        h = ctypes.c_void_p()
+        _lib.check(L.qres_create(ctypes.byref(cfg), rank, nranks, ctypes.byref(h)), None, "qres_create")
+        self.ctx = h
+        self._keep = []
+        dev = self.device
+        # ---- weights: the rank's slices, re-laid for the GEMV
+        self.w_gdn = [shard(g["Win"], d.gdn_rows()) for g in w["gdn"]] if self.n_gdn else []
+        self.gdn_params = [
+            dict(
+                taps=g["taps"][d.conv_channels().to(g["taps"].device)].contiguous().to(dev),
+                dt=g["dt"][d.r * d.nv : (d.r + 1) * d.nv].contiguous().to(dev),
+                neg_a=g["neg_a"][d.r * d.nv : (d.r + 1) * d.nv].contiguous().to(dev),
+                norm_w=g["norm_w"].float().contiguous().to(dev),
+            )
+            for g in (w["gdn"] if self.n_gdn else [])
+        ]
+        self.w_attn = [shard(a["Win"], d.attn_rows()) for a in w["attn"]] if self.n_attn else []
+        self.attn_params = [
+            dict(wq=(a["wq"].float() / math.sqrt(HD)).contiguous().to(dev), wk=a["wk"].float().contiguous().to(dev))
+            for a in (w["attn"] if self.n_attn else [])
+        ]
+        self.w_out = [shard(o, None, d.mixer_k()) for o in w["out"]]
+        self.w_gu = [shard(stack_matrices(m["G"], m["U"]), d.gateup_rows()) for m in w["mlp"]]
+        self.w_down = [shard(m["D"], None, d.mlp_k()) for m in w["mlp"]]
+        self.w_head = shard(w["head"], d.vocab_rows()) if self.lm_head else None
+        self.weight_bytes = self._count_weight_bytes()
+        # ---- decode state (per state copy)
+        R = batch
+        self.gdn_state = [torch.zeros(R, d.nv, DK, DV, device=dev) for _ in range(self.state_copies[0])]
+        self.conv_hist = [
+            torch.zeros(R, _lib.QRES_HIST_SLOTS, d.conv, dtype=torch.bfloat16, device=dev)
+            for _ in range(self.state_copies[0])
+        ]
+        npages = R * self.max_pages
+        self.k_pool = [torch.zeros(npages, d.nkv, 64, HD, dtype=torch.bfloat16, device=dev) for _ in range(self.state_copies[1])]
+        self.v_pool = [torch.zeros(npages, d.nkv, 64, HD, dtype=torch.bfloat16, device=dev) for _ in range(self.state_copies[1])]
+        if page_table is None:
+            page_table = torch.arange(npages, dtype=torch.int32).view(R, self.max_pages)
+        self.page_table = page_table.to(torch.int32).to(dev).contiguous()
+        # ---- io
+        self.tok_d = torch.zeros(_lib.TOK_WORDS, dtype=torch.int32, device=dev)
+        self.x0_d = torch.zeros(R, HIDDEN, device=dev)
+        self.x_d = torch.zeros(R, HIDDEN, device=dev)
+        self.logits_d = torch.zeros(R, max(d.vocab, 1), dtype=torch.bfloat16, device=dev)
+        self.topk_d = torch.zeros(R, 2 * TOP_K, dtype=torch.int32, device=dev)
+        self.out_d = torch.zeros(R, 4, dtype=torch.int32, device=dev)
+        self.mixer_d = torch.zeros(R, d.gv, dtype=torch.bfloat16, device=dev)
+        self.embed = embed.to(dev).bfloat16().contiguous() if embed is not None else None
+        cos, sin = rope_table(max_pos)
+        self.cos_d, self.sin_d = cos.to(dev), sin.to(dev)
+        # ---- bind
+        self._bind()
+        sz = ctypes.c_size_t()
+        _lib.check(L.qres_workspace_size(self.ctx, ctypes.byref(sz)), self.ctx, "workspace size")
+        self.ws = torch.zeros(sz.value, dtype=torch.uint8, device=dev)
+        _lib.check(L.qres_bind_workspace(self.ctx, _lib.ptr(self.ws), sz.value), self.ctx, "bind workspace")
+        if nranks > 1:
+            if nccl_id is None:
+                raise ValueError("nranks > 1 needs the NCCL id (see nccl_unique_id)")
+            buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            _lib.check(L.qres_nccl_init(self.ctx, None, buf), self.ctx, "nccl init")
+        self.trace = False
+        self._initial = None
+
+    # ------------------------------------------------------------------------------------------ binding
+    def _layer_copy(self, l):
+        """(kind copy, state copy) of layer l: the k-th layer of its kind uses copy k % copies"""
+        k = sum(is_attn(j, self.interval) == is_attn(l, self.interval) for j in range(l))
+        if is_attn(l, self.interval):
+            return k % len(self.w_attn), k % self.state_copies[1]
+        return k % len(self.w_gdn), k % self.state_copies[0]
+
+    def _bind(self):
+        L, c = _lib.lib(), self.ctx
+        for l in range(self.layers):
+            wc, sc = self._layer_copy(l)
+            m = l % len(self.w_out)
+            if is_attn(l, self.interval):
+                _lib.check(L.qres_load_weights(c, l, _lib.W_ATTN_IN, ctypes.byref(self.w_attn[wc].cstruct())), c, "w")
+                p = self.attn_params[wc]
+                _lib.check(L.qres_load_attn_params(c, l, _lib.ptr(p["wq"]), _lib.ptr(p["wk"])), c, "attn params")
+                st = _lib.LayerState(0, 0, self.k_pool[sc].data_ptr(), self.v_pool[sc].data_ptr())
+            else:
+                _lib.check(L.qres_load_weights(c, l, _lib.W_GDN_IN, ctypes.byref(self.w_gdn[wc].cstruct())), c, "w")
+                p = self.gdn_params[wc]
+                _lib.check(
+                    L.qres_load_gdn_params(c, l, _lib.ptr(p["taps"]), _lib.ptr(p["dt"]), _lib.ptr(p["neg_a"]), _lib.ptr(p["norm_w"])),
+                    c,
+                    "gdn params",
+                )
+                st = _lib.LayerState(self.gdn_state[sc].data_ptr(), self.conv_hist[sc].data_ptr(), 0, 0)
+            _lib.check(L.qres_bind_state(c, l, ctypes.byref(st)), c, "state")
+            _lib.check(L.qres_load_weights(c, l, _lib.W_OUT, ctypes.byref(self.w_out[m].cstruct())), c, "w out")
+            _lib.check(L.qres_load_weights(c, l, _lib.W_GATEUP, ctypes.byref(self.w_gu[m].cstruct())), c, "w gu")
+            _lib.check(L.qres_load_weights(c, l, _lib.W_DOWN, ctypes.byref(self.w_down[m].cstruct())), c, "w down")
+        if self.lm_head:
+            _lib.check(L.qres_load_weights(c, -1, _lib.W_HEAD, ctypes.byref(self.w_head.cstruct())), c, "w head")
+        _lib.check(L.qres_bind_rope(c, _lib.ptr(self.cos_d), _lib.ptr(self.sin_d), self.max_pos), c, "rope")
+        io = _lib.Io(
+            self.tok_d.data_ptr(),
+            self.x0_d.data_ptr(),
+            self.embed.data_ptr() if self.embed is not None else 0,
+            self.page_table.data_ptr(),
+            self.x_d.data_ptr(),
+            self.logits_d.data_ptr() if self.lm_head else 0,
+            self.topk_d.data_ptr() if self.lm_head else 0,
+            self.out_d.data_ptr() if self.lm_head else 0,
+            self.mixer_d.data_ptr(),
+        )
+        _lib.check(L.qres_bind_io(c, ctypes.byref(io)), c, "io")
+
+    def _count_weight_bytes(self):
+        """algorithmic weight bytes one step streams on this rank (FP8 + 4 B per 128x128 block)"""
+        b = 0
+        for l in range(self.layers):
+            wc, _ = self._layer_copy(l)
+            m = l % len(self.w_out)
+            b += (self.w_attn[wc] if is_attn(l, self.interval) else self.w_gdn[wc]).nbytes
+            b += self.w_out[m].nbytes + self.w_gu[m].nbytes + self.w_down[m].nbytes
+        if self.lm_head:
+            b += self.w_head.nbytes
+        return b
+
+    def state_bytes_per_step(self, ctx=None):
+        """algorithmic decode-state bytes of one step on this rank: GDN states read + written, conv history
+        (3 rows read, 1 written), KV rows read (ctx positions per attention layer) -- per user"""
+        d = self.d
+        ctx = ctx if ctx is not None else self.max_pos // 2
+        gdn = self.n_gdn * (2 * d.nv * DK * DV * 4 + 4 * d.conv * 2)
+        kv = self.n_attn * (ctx + 1) * d.nkv * HD * 2 * 2
+        return self.batch * (gdn + kv)
+
+    # ------------------------------------------------------------------------------------------ token state
+    def token_state(self, x0=None, pos=0, tokens=None, feed=False):
+        """host token state (model.py:1314-1351): x0 [HIDDEN] or [batch, HIDDEN] rows (bf16 values) or token ids
+        (gathered from the embedding on device), at position(s) pos. Returns (words int32 [40], x0 or None)."""
+        B = self.batch
+        pos = [pos] * B if not isinstance(pos, (list, tuple)) else list(pos)
+        assert len(pos) == B and all(0 <= p < self.max_pos for p in pos), pos
+        words = torch.zeros(_lib.TOK_WORDS, dtype=torch.int32)
+        words[_lib.TOK_POS : _lib.TOK_POS + B] = torch.tensor(pos, dtype=torch.int32)
+        if tokens is not None:
+            tokens = [tokens] * B if not isinstance(tokens, (list, tuple)) else list(tokens)
+            assert self.embed is not None, "token rows need the embedding table"
+            words[_lib.TOK_TOKEN : _lib.TOK_TOKEN + B] = torch.tensor(tokens, dtype=torch.int32)
+            xr = None
+        else:
+            words[_lib.TOK_TOKEN : _lib.TOK_TOKEN + B] = -1
+            xr = x0.reshape(B, HIDDEN).float()
+        words[_lib.TOK_FEED] = int(feed)
+        return words, xr
+
+    def write_token_state(self, tok):
+        words, xr = tok
+        self.tok_d.copy_(words, non_blocking=True)
+        if xr is not None:
+            self.x0_d.copy_(xr, non_blocking=True)
+
+    def step(self, tok=None, stream=None):
+        """one decode step (async); tok None: continue from the token state the previous step fed (feed mode)"""
+        if tok is not None:
+            self.write_token_state(tok)
+        s = _lib.stream_ptr(stream)
+        L = _lib.lib()
+        if self.trace:
+            _lib.check(L.qres_replay(self.ctx, s), self.ctx, "replay")
+        else:
+            _lib.check(L.qres_decode_step(self.ctx, s), self.ctx, "decode step")
+
+    def check(self, stream=None):
+        """synchronise and raise if a kernel of the step reported an error (timeout / index out of range)"""
+        _lib.check(_lib.lib().qres_check(self.ctx, _lib.stream_ptr(stream)), self.ctx, "device")
+
+    @property
+    def launches(self):
+        """kernels of libqres one step launches"""
+        return _lib.lib().qres_step_launches(self.ctx)
+
+    def capture_trace(self, stream=None):
+        """record one step as a CUDA graph (model.py:1485-1492); step() then replays it"""
+        s = stream or torch.cuda.Stream(device=self.device)
+        torch.cuda.synchronize(self.device)
+        _lib.check(_lib.lib().qres_capture(self.ctx, _lib.stream_ptr(s)), self.ctx, "capture")
+        torch.cuda.synchronize(self.device)
+        self.trace = True
+
+    def release_trace(self):
+        if self.trace:
+            _lib.lib().qres_release_graph(self.ctx)
+            self.trace = False
+
+    # ------------------------------------------------------------------------------------------ results
+    def x(self):
+        """x after the step: [HIDDEN] or [batch, HIDDEN]"""
+        x = self.x_d.float().cpu()
+        return x[0] if self.batch == 1 else x
+
+    def mixer_output(self):
+        """the last layer's mixer output (the out-projection's bf16 input) of this rank: [gv] or [batch, gv]"""
+        o = self.mixer_d.float().cpu()
+        return o[0] if self.batch == 1 else o
+
+    def logits(self):
+        """this rank's logits [vocab / n] (bf16 values) or [batch, vocab / n]"""
+        lg = self.logits_d.float().cpu()
+        return lg[0] if self.batch == 1 else lg
+
+    def topk(self):
+        """the merged top-32 list per row: (keys [batch, 32], vocab indices [batch, 32])"""
+        t = self.topk_d.cpu().to(torch.int64) & 0xFFFFFFFF
+        return t[:, :TOP_K], t[:, TOP_K:]
+
+    def argmax(self):
+        """vocab index of the largest logit, the smallest index on ties (model.py:1558-1573); a list for batch > 1"""
+        a = self.out_d[:, 0].cpu().tolist()
+        return a[0] if self.batch == 1 else a
+
+    def fed_token(self):
+        """(token, position) the last step fed into the next one"""
+        o = self.out_d[0].cpu().tolist()
+        return int(o[0]), int(o[1])
+
+    # ------------------------------------------------------------------------------------------ state
+    def load_state(self, st, user=0):
+        """write a decode state (attributes pos, gdn [copies][48,128,128], hist [copies][3, 10240] for positions
+        pos-3..pos-1, K / V [copies][4, max_pos, 256]) as user `user`'s (model.py:1447-1470)"""
+        d, dev = self.d, self.device
+        ch = d.conv_channels()
+        for c in range(self.state_copies[0]):
+            if c < len(st.gdn):
+                self.gdn_state[c][user].copy_(st.gdn[c][d.r * d.nv : (d.r + 1) * d.nv].to(dev))
+                h = st.hist[c][:, ch].to(dev).bfloat16()
+                for age in range(3):
+                    slot = (st.pos - 3 + age) % _lib.QRES_HIST_SLOTS
+                    self.conv_hist[c][user, slot] = h[age]
+        for c in range(self.state_copies[1]):
+            if c < len(st.K):
+                P = min(st.pos, st.K[c].shape[1])
+                pt = self.page_table[user].cpu()
+                for kv, pool in ((st.K[c], self.k_pool[c]), (st.V[c], self.v_pool[c])):
+                    src = kv[d.kv0 : d.kv0 + d.nkv, :P].to(dev).bfloat16()  # [nkv, P, 256]
+                    npg = -(-P // 64)
+                    padded = torch.zeros(d.nkv, npg * 64, HD, dtype=torch.bfloat16, device=dev)
+                    padded[:, :P] = src
+                    pages = padded.view(d.nkv, npg, 64, HD).permute(1, 0, 2, 3)
+                    pool[pt[:npg].long().to(dev)] = pages
+        torch.cuda.synchronize(dev)
+
+    def dump_gdn_state(self, copy=0, user=0):
+        return self.gdn_state[copy][user].cpu()
+
+    def kv_rows(self, copy, positions, user=0, which="K"):
+        """rows of the paged cache at positions: [nkv, len, 256] float"""
+        pool = (self.k_pool if which == "K" else self.v_pool)[copy]
+        pt = self.page_table[user].cpu()
+        out = [pool[int(pt[p // 64]), :, p % 64].float().cpu() for p in positions]
+        return torch.stack(out, 1)
+
+    def reset(self):
+        """zero the decode state (GDN states, conv histories, KV pools)"""
+        for t in self.gdn_state + self.conv_hist + self.k_pool + self.v_pool:
+            t.zero_()
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.release_trace()
+            _lib.lib().qres_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def nccl_unique_id():
+    """128-byte NCCL id for the ranks' communicator (rank 0 makes it; the caller broadcasts it)"""
+    buf = ctypes.create_string_buffer(128)
+    _lib.check(_lib.lib().qres_nccl_unique_id(None, buf), None, "nccl id")
+    return bytes(buf.raw)
