@@ -184,7 +184,8 @@ def attn_mixer(y, s, wq, wk, K_all, V_all, pos, cos, sin):
 def torch_step(x0, P, st, layers, interval, lm_head=False, mixer_out=None):
     """one decode step of one user at st.pos over Prepared weights P; updates st (GDN states, conv histories,
     KV rows at pos) in place and returns x (and the per-rank logits with lm_head). mixer_out: a list that
-    receives (layer, rank, o) per mixer, o the bf16 input of the out-projection"""
+    receives (layer, rank, o) per mixer, o the bf16 input of the out-projection. The k-th layer of a kind uses
+    weight copy k % len(weights) and state copy k % len(states) (the reference uses one count for both)."""
     pos = st.pos
     cos, sin = rope_tables(pos)
     x = x0.clone()
@@ -195,22 +196,24 @@ def torch_step(x0, P, st, layers, interval, lm_head=False, mixer_out=None):
         parts = []
         if is_attn(l, interval):
             c = a_i % len(w.attn)
+            cs = a_i % len(st.K)  # the state copy (= the weight copy when their counts match, as in the reference)
             wa = w.attn[c]
             for r, s in enumerate(P.sh):
                 y = bf16(h @ P.attn[c][r])
-                o = attn_mixer(y, s, wa["wq"], wa["wk"], st.K[c], st.V[c], pos, cos, sin)
+                o = attn_mixer(y, s, wa["wq"], wa["wk"], st.K[cs], st.V[cs], pos, cos, sin)
                 if mixer_out is not None:
                     mixer_out.append((l, r, o))
                 parts.append(o @ P.out[l % len(w.out)][r] + (x if r == 0 else 0))
             a_i += 1
         else:
             c = g_i % len(w.gdn)
+            cs = g_i % len(st.gdn)
             wg = w.gdn[c]
             for r, s in enumerate(P.sh):
                 y = bf16(h @ P.gdn[c][r]["Win"])
                 ch = s.conv_channels()
-                hist = st.hist[c][:, ch]
-                o, st.hist[c][:, ch] = gdn_mixer(y, s, P.gdn[c][r]["taps"], wg, hist, st.gdn[c])
+                hist = st.hist[cs][:, ch]
+                o, st.hist[cs][:, ch] = gdn_mixer(y, s, P.gdn[c][r]["taps"], wg, hist, st.gdn[cs])
                 if mixer_out is not None:
                     mixer_out.append((l, r, o))
                 parts.append(o @ P.out[l % len(w.out)][r] + (x if r == 0 else 0))

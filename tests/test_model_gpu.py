@@ -3,6 +3,10 @@ consecutive steps of G G G A G G G A + lm_head (tests/bench_resident_model.py:48
 replay bit-identical to eager steps (test_resident_accuracy.py:223-258), device-fed greedy == host-fed greedy
 (test_resident_feed.py:370-436).
 
+Every layer has its own decode state here (weights may be shared copies): the reference's shared state copies
+shift one conv history several times per step, a test economy that a position-keyed history ring does not
+model.
+
 Tolerances: per step the device and the oracle start from the same state (the oracle state is reloaded into the
 model before every step), so errors do not compound: x and the logits within 2e-2 relative (BASELINE atol 2e-2
 on bf16 activations; the oracle itself moves by ~0.5% between equally valid fp32 orders, see
@@ -58,9 +62,8 @@ def rel(a, b):
 def test_decode_steps_parity(cuda, setup8):
     w8, P = setup8
     layers, interval, pos = 8, 4, 100
-    st = refgen.random_state(2, 1, pos, pos + 64, seed=1)
-    model = ResidentModel(weights.canonical_from_fp8(w8), layers, interval, batch=1, max_pos=pos + 64, lm_head=True,
-                          state_copies=(2, 1))
+    st = refgen.random_state(6, 2, pos, pos + 64, seed=1)
+    model = ResidentModel(weights.canonical_from_fp8(w8), layers, interval, batch=1, max_pos=pos + 64, lm_head=True)
     g = torch.Generator().manual_seed(7)
     for s in range(3):
         model.load_state(st)
@@ -87,7 +90,7 @@ def test_decode_steps_parity(cuda, setup8):
     model.step(model.token_state(x0, ref.pos))
     model.check()
     step.torch_step(x0, P, ref, layers, interval, lm_head=True)
-    for c in range(2):
+    for c in range(6):
         assert rel(model.dump_gdn_state(c), ref.gdn[c]) < 2e-2
     k = model.kv_rows(0, [st.pos])[:, 0]
     assert rel(k, ref.K[0][:, st.pos]) < 2e-2
@@ -96,9 +99,8 @@ def test_decode_steps_parity(cuda, setup8):
 def test_graph_replay_bitidentical_and_deterministic(cuda, setup8):
     w8, _ = setup8
     pos = 40
-    st = refgen.random_state(2, 1, pos, pos + 64, seed=1)
-    model = ResidentModel(weights.canonical_from_fp8(w8), 8, 4, batch=1, max_pos=pos + 64, lm_head=True,
-                          state_copies=(2, 1))
+    st = refgen.random_state(6, 2, pos, pos + 64, seed=1)
+    model = ResidentModel(weights.canonical_from_fp8(w8), 8, 4, batch=1, max_pos=pos + 64, lm_head=True)
     g = torch.Generator().manual_seed(5)
     xs = [torch.randn(5120, generator=g).bfloat16().float() for _ in range(4)]
 
@@ -125,9 +127,8 @@ def test_device_fed_greedy_equals_host_fed(cuda, setup8):
     w8, _ = setup8
     vocab = 16384
     emb = (torch.randn(vocab, 5120, generator=torch.Generator().manual_seed(9))).bfloat16()
-    st = refgen.random_state(2, 1, 0, 64, seed=1, zero=True)
-    model = ResidentModel(weights.canonical_from_fp8(w8), 8, 4, batch=1, max_pos=64, lm_head=True,
-                          state_copies=(2, 1), embed=emb)
+    st = refgen.random_state(6, 2, 0, 64, seed=1, zero=True)
+    model = ResidentModel(weights.canonical_from_fp8(w8), 8, 4, batch=1, max_pos=64, lm_head=True, embed=emb)
     # host-fed: the host reads each argmax and writes the next token state
     model.load_state(st)
     tok, host = 17, []
@@ -150,3 +151,23 @@ def test_device_fed_greedy_equals_host_fed(cuda, setup8):
         fed.append(t)
     model.release_trace()
     assert fed == host
+
+
+@pytest.mark.parametrize("layers,interval", [(1, 0), (1, 1), (2, 2), (4, 4)])
+def test_layer_schedules_parity(cuda, setup8, layers, interval):
+    """short schedules (one GDN layer, one attention layer, G A, G G G A) from the same start state: localises a
+    mismatch to a layer kind"""
+    w8, P = setup8
+    pos = 70
+    n_attn = sum(step.is_attn(l, interval) for l in range(layers))
+    st = refgen.random_state(layers - n_attn, n_attn, pos, pos + 64, seed=1)
+    model = ResidentModel(weights.canonical_from_fp8(w8), layers, interval, batch=1, max_pos=pos + 64, lm_head=True)
+    model.load_state(st)
+    x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
+    model.step(model.token_state(x0, st.pos))
+    model.check()
+    mix = []
+    x_ref, lg = step.torch_step(x0, P, st, layers, interval, lm_head=True, mixer_out=mix)
+    o_ref = torch.cat([o for l, _, o in mix if l == layers - 1])
+    errs = (rel(model.mixer_output(), o_ref), rel(model.x(), x_ref), rel(model.logits(), step.logits_bf16(lg)))
+    assert max(errs) < 2e-2, errs

@@ -102,7 +102,7 @@ class Io(ctypes.Structure):
     ]
 
 
-TOK_WORDS = 40  # sizeof(qres_tok) / 4: pos[8], token[8], feed, step, reserved[14]
+TOK_WORDS = 32  # sizeof(qres_tok) / 4: pos[8], token[8], feed, step, reserved[14]
 TOK_POS, TOK_TOKEN, TOK_FEED, TOK_STEP = 0, 8, 16, 17
 
 _lib = None

@@ -211,7 +211,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             const int j = warp;
             const float s0 = sc[j][lane], s1 = sc[j][lane + 32];
             const float mx = warp_max(fmaxf(s0, s1));
-            const float mnew = fmaxf(mrow[j] * 0.f + (i == 0 ? -INFINITY : mrow[j]), mx);
+            const float mprev = i == 0 ? -INFINITY : mrow[j];
+            const float mnew = fmaxf(mprev, mx);
             const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - mnew);
             const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - mnew);
             sc[j][lane] = p0;

@@ -300,9 +300,9 @@ static cudaError_t launch_b(const GemvParams& p, int grid, size_t smem, cudaStre
     auto k = gemv_fp8_kernel<B, PRO, EPI>;
     static size_t smem_set = 0;  // largest dynamic shared memory opted in so far for this instantiation
     if (smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        smem_set = 227 * 1024;
+        smem_set = smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

@@ -210,7 +210,7 @@ class ResidentModel:
     # ------------------------------------------------------------------------------------------ token state
     def token_state(self, x0=None, pos=0, tokens=None, feed=False):
         """host token state (model.py:1314-1351): x0 [HIDDEN] or [batch, HIDDEN] rows (bf16 values) or token ids
-        (gathered from the embedding on device), at position(s) pos. Returns (words int32 [40], x0 or None)."""
+        (gathered from the embedding on device), at position(s) pos. Returns (words int32 [32], x0 or None)."""
         B = self.batch
         pos = [pos] * B if not isinstance(pos, (list, tuple)) else list(pos)
         assert len(pos) == B and all(0 <= p < self.max_pos for p in pos), pos
