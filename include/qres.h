@@ -59,21 +59,22 @@ typedef struct {
     int32_t rows;          /* users per step, 1..QRES_MAX_ROWS */
     int32_t max_pages;     /* page-table entries per user */
     int32_t num_pages;     /* pages in each attention layer's K (and V) pool */
-    int32_t sm_count;      /* CTAs of the weight-streaming kernels; 0 = the device's SM count */
+    int32_t sm_count;      /* SMs to use; 0 = the device's (the weight-streaming kernels run 2 CTAs per SM) */
     int32_t flags;         /* reserved, 0 */
 } qres_config;
 
-/* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block), in the GEMV layout made by
- * qres_tile_weight: rows in quads of 4, each quad's K split into chunks of 512, a chunk stored as its 4 rows
- * back to back. sidx maps every (padded) row to its row of the scale table. */
+/* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block of the canonical matrix), in the
+ * GEMV layout made by qres_tile_weight: rows in tiles of 16 (zero-padded), a tile's K in 128-wide units of 2 KB
+ * stored back to back, inside a unit row r at r * 128 with its two 64-byte halves swapped when r is odd.
+ * uscale gives every unit its block scales: .x for the unit's rows with r % 4 < 2, .y for r % 4 >= 2 (the two
+ * halves of a gate|up quad; equal elsewhere). */
 typedef struct {
     const void* data;      /* rows_pad * K bytes */
-    const float* scales;   /* [n_scale_rows][K / 128] */
-    const int32_t* sidx;   /* [rows_pad], non-decreasing */
+    const float* uscale;   /* [rows_pad / 16][K / 128][2] */
     int32_t rows;          /* real rows */
-    int32_t rows_pad;      /* rows rounded up to a multiple of 4 */
+    int32_t rows_pad;      /* rows rounded up to a multiple of 16 */
     int32_t K;             /* multiple of 128 */
-    int32_t n_scale_rows;
+    int32_t reserved;
 } qres_weight;
 
 /* per-layer decode state (State, model.py:151-174), laid out for this rank */
@@ -158,9 +159,11 @@ QRES_API int32_t qres_step_launches(const qres_ctx* ctx);
 /* ---- single kernels (the building blocks of a step, for tests and microbenchmarks) ---- */
 /* y = act(h @ W^T) for `rows` users: pro 0 = h = bf16(rmsnorm(x)) from fp32 x [rows][K]; pro 1 = h = bf16
  * input [rows][K]. epi 0 = bf16 out [rows][w.rows]; 1 = SwiGLU over interleaved gate|up pairs, bf16 out
- * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid 0 = the SM count. */
+ * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid 0 = twice the SM count.
+ * work: qres_gemv_workspace_size bytes (split-tile partials and tickets), zeroed once before first use. */
+QRES_API qres_status qres_gemv_workspace_size(int32_t grid, int32_t rows_pad, size_t* bytes);
 QRES_API qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
-                      int32_t grid, uint32_t* err, void* stream);
+                      int32_t grid, uint32_t* err, void* work, size_t work_bytes, void* stream);
 /* One GDN mixer (streamer conv1d+SiLU model.py:255-258 and gdn_head_compute.cpp) for `rows` users at the
  * positions in pos[] (device): y [rows][ld_y] in-projection rows -> o [rows][6144/n] bf16. */
 QRES_API qres_status qres_gdn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int32_t ld_y, const int32_t* pos,
@@ -184,7 +187,7 @@ QRES_API qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_l
 /* ---- weight preparation ---- */
 /* fp32 [N][K] -> e4m3 bytes [N][K] + scales [ceil(N/128)][K/128] (amax / 448 per 128 x 128 block). */
 QRES_API qres_status qres_quantize_fp8(const float* w, int32_t N, int32_t K, uint8_t* q, float* scales, void* stream);
-/* row-major e4m3 [rows][K] -> the GEMV layout of qres_weight (rows_pad = rows rounded up to 4, zero rows). */
+/* row-major e4m3 [rows][K] -> the GEMV layout of qres_weight (rows_pad = rows rounded up to 16, zero rows). */
 QRES_API qres_status qres_tile_weight(const uint8_t* src, int32_t rows, int32_t K, uint8_t* dst, void* stream);
 
 #ifdef __cplusplus

@@ -55,17 +55,19 @@ def test_quantize_bitexact(cuda):
 
 def test_tile_layout_bitexact(cuda):
     g = torch.Generator().manual_seed(1)
-    for rows, K in ((10, 640), (8, 768), (5, 2176)):
+    for rows, K in ((10, 640), (40, 768), (5, 2176)):
         q = torch.randint(0, 255, (rows, K), generator=g, dtype=torch.uint8)
-        t = _lib.tile_weight(q.to(cuda)).cpu()
-        rows_pad = (rows + 3) // 4 * 4
+        q_d = q.to(cuda)
+        t = _lib.tile_weight(q_d).cpu()
+        rows_pad = (rows + 15) // 16 * 16
         qp = torch.zeros(rows_pad, K, dtype=torch.uint8)
         qp[:rows] = q
         ref = []
-        for quad in range(rows_pad // 4):
-            for c in range(-(-K // 512)):
-                wc = min(512, K - 512 * c)
-                ref.append(qp[4 * quad : 4 * quad + 4, 512 * c : 512 * c + wc].reshape(-1))
+        for tile in range(rows_pad // 16):
+            for kb in range(K // 128):
+                for r in range(16):
+                    row = qp[16 * tile + r, 128 * kb : 128 * kb + 128]
+                    ref.append(torch.cat([row[64:], row[:64]]) if r % 2 else row)
         assert torch.equal(t, torch.cat(ref))
 
 

@@ -39,6 +39,7 @@ EXPORTS = [
     "qres_release_graph",
     "qres_check",
     "qres_step_launches",
+    "qres_gemv_workspace_size",
     "qres_gemv",
     "qres_gdn_mixer",
     "qres_attn_workspace_size",
@@ -70,12 +71,11 @@ class Config(ctypes.Structure):
 class Weight(ctypes.Structure):
     _fields_ = [
         ("data", ctypes.c_void_p),
-        ("scales", ctypes.c_void_p),
-        ("sidx", ctypes.c_void_p),
+        ("uscale", ctypes.c_void_p),
         ("rows", ctypes.c_int32),
         ("rows_pad", ctypes.c_int32),
         ("K", ctypes.c_int32),
-        ("n_scale_rows", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -135,7 +135,8 @@ def lib():
             "qres_replay": [vp, vp],
             "qres_release_graph": [vp],
             "qres_check": [vp, vp],
-            "qres_gemv": [ctypes.POINTER(Weight), i32, i32, vp, i32, vp, i32, vp, vp],
+            "qres_gemv_workspace_size": [i32, i32, ctypes.POINTER(sz)],
+            "qres_gemv": [ctypes.POINTER(Weight), i32, i32, vp, i32, vp, i32, vp, vp, sz, vp],
             "qres_gdn_mixer": [i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
             "qres_attn_workspace_size": [i32, i32, i32, ctypes.POINTER(sz)],
             "qres_attn_mixer": [i32, i32, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp],
@@ -175,12 +176,29 @@ def stream_ptr(stream=None):
 
 
 # ------------------------------------------------------------------------------ single-kernel ops (torch.ops.qres)
-def gemv(w, h, pro, epi, out, err=None, grid=0, stream=None):
+_gemv_work = {}
+
+
+def gemv_work(device, rows_pad, grid=0):
+    """a zeroed GEMV workspace for weights of up to rows_pad rows (cached per device)"""
+    sz = ctypes.c_size_t()
+    check(lib().qres_gemv_workspace_size(grid, rows_pad, ctypes.byref(sz)), None, "gemv ws")
+    key = (str(device), grid)
+    w = _gemv_work.get(key)
+    if w is None or w.numel() < sz.value:
+        w = torch.zeros(sz.value, dtype=torch.uint8, device=device)
+        _gemv_work[key] = w
+    return w
+
+
+def gemv(w, h, pro, epi, out, err=None, grid=0, stream=None, work=None):
     """one weight-streaming projection (see qres_gemv); w a GemvWeight, h [rows][K] (fp32 x or bf16), out
     preallocated"""
     rows = h.shape[0]
+    work = work if work is not None else gemv_work(h.device, w.rows_pad, grid)
     check(
-        lib().qres_gemv(ctypes.byref(w.cstruct()), rows, pro, ptr(h), epi, ptr(out), grid, ptr(err), stream_ptr(stream)),
+        lib().qres_gemv(ctypes.byref(w.cstruct()), rows, pro, ptr(h), epi, ptr(out), grid, ptr(err), ptr(work),
+                        work.numel(), stream_ptr(stream)),
         None,
         "qres_gemv",
     )
@@ -197,9 +215,9 @@ def quantize_fp8(w, stream=None):
 
 
 def tile_weight(q, stream=None):
-    """row-major e4m3 [rows][K] (device) -> the GEMV layout (rows padded to a multiple of 4)"""
+    """row-major e4m3 [rows][K] (device) -> the GEMV layout (rows padded to a multiple of 16)"""
     rows, K = q.shape
-    rows_pad = (rows + 3) // 4 * 4
+    rows_pad = (rows + 15) // 16 * 16
     dst = torch.empty(rows_pad * K, dtype=torch.uint8, device=q.device)
     check(lib().qres_tile_weight(ptr(q.contiguous()), rows, K, ptr(dst), stream_ptr(stream)), None, "tile")
     return dst

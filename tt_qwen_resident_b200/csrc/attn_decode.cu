@@ -41,6 +41,8 @@ struct AttnParams {
     float* part;              // [B][nkv][nchunks][G][2 + 256]
     int* ticket;              // [B][nkv]
     int nchunks;
+    const uint8_t* pf;        // the next projection's weights: prefetched into L2 while this kernel runs
+    size_t pf_bytes;
     uint32_t* err;
 };
 
@@ -100,6 +102,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     }
     __syncthreads();
     pdl_launch();
+    if (p.pf && tid == 0) {
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
+    }
     pdl_wait();
 
     const int pos = p.pos[b];
@@ -270,23 +276,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate
+    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate. The chunk
+    // weights are computed once in shared memory; every thread then sums its dimension over the chunks with
+    // independent loads.
     const float* base = p.part + (((size_t)b * p.nkv + g) * p.nchunks) * G * (2 + kHD);
-    for (int j = 0; j < G; ++j) {
+    float* wch = reinterpret_cast<float*>(ring);  // [nchunks][G] chunk weights (the K/V ring is free now)
+    for (int i = tid; i < p.nchunks * G; i += kAttnThreads) wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
+    __syncthreads();
+    if (tid < G) {
         float M = -INFINITY;
-        for (int cc = 0; cc < p.nchunks; ++cc) M = fmaxf(M, __ldcg(base + ((size_t)cc * G + j) * (2 + kHD)));
-        float Lsum = 0.f, O = 0.f;
+        for (int cc = 0; cc < p.nchunks; ++cc) M = fmaxf(M, wch[cc * G + tid]);
+        float Lsum = 0.f;
         for (int cc = 0; cc < p.nchunks; ++cc) {
-            const float* pc = base + ((size_t)cc * G + j) * (2 + kHD);
-            const float mc = __ldcg(pc);
-            if (mc == -INFINITY) continue;
-            const float w = expf(mc - M);
-            Lsum = fmaf(w, __ldcg(pc + 1), Lsum);
-            O = fmaf(w, __ldcg(pc + 2 + tid), O);
+            const float mc = wch[cc * G + tid];
+            const float w = mc == -INFINITY ? 0.f : expf(mc - M);
+            wch[cc * G + tid] = w;
+            Lsum = fmaf(w, __ldcg(base + ((size_t)cc * G + tid) * (2 + kHD) + 1), Lsum);
+        }
+        lrow[tid] = Lsum;
+    }
+    __syncthreads();
+    for (int j = 0; j < G; ++j) {
+        float O = 0.f;
+#pragma unroll 8
+        for (int cc = 0; cc < p.nchunks; ++cc) {
+            const float w = wch[cc * G + j];
+            if (w != 0.f) O = fmaf(w, __ldcg(base + ((size_t)cc * G + j) * (2 + kHD) + 2 + tid), O);
         }
         const int hq = g * G + j;
         const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);
-        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(O / Lsum, sigmoid_f(gate)));
+        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(O / lrow[j], sigmoid_f(gate)));
         const size_t idx = (size_t)b * p.h * kHD + hq * kHD + tid;
         reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
         if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
@@ -311,7 +330,8 @@ int attn_default_chunks(int nranks, int rows, int sm_count, int max_pages) {
 cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const int32_t* page_table,
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
-                        void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl) {
+                        void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
+                        const void* pf, size_t pf_bytes) {
     if (nranks < 1 || 24 % nranks || rows < 1 || rows > kMaxRows) return cudaErrorInvalidValue;
     if (work_bytes < attn_workspace_bytes(nranks, rows, nchunks)) return cudaErrorInvalidValue;
     AttnParams p;
@@ -338,6 +358,8 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
     p.part = static_cast<float*>(work);
     p.ticket = reinterpret_cast<int*>(static_cast<uint8_t*>(work) + part + 256);
     p.nchunks = nchunks;
+    p.pf = static_cast<const uint8_t*>(pf);
+    p.pf_bytes = pf_bytes;
     p.err = err;
     const size_t smem = attn_smem_bytes();
     cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -1,5 +1,5 @@
 // Small kernels of the decode step and weight preparation for sm_100a:
-//  - tile_weight: row-major e4m3 [rows][K] -> the GEMV quad/chunk layout (gemv_fp8.cu);
+//  - tile_weight: row-major e4m3 [rows][K] -> the GEMV tile/unit layout (gemv_fp8.cu);
 //  - quantize_fp8: fp32 [N][K] -> e4m3 + one fp32 scale per 128 x 128 block (amax / 448);
 //  - topk: per-row top-32 (key, index) list and argmax of bf16 logits, the order and tie rule of the
 //    reference's sampling.hpp (:24-74): bf16 order keys descending, the smaller vocab index first on ties;
@@ -10,20 +10,21 @@
 namespace qres {
 
 // ------------------------------------------------------------------------------------------------ tiling
+// dst[(T * nkb + kb) * 2048 + r * 128 + ((half ^ (r & 1)) * 64) + i] = src[(16 T + r) * K + kb * 128 + half * 64 + i]
 __global__ void tile_weight_kernel(const uint8_t* __restrict__ src, int rows, int K, uint8_t* __restrict__ dst,
                                    size_t total16) {
-    // one 16-byte vector of the destination per thread
+    const int nkb = K / 128;
     for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < total16; v += (size_t)gridDim.x * blockDim.x) {
         const size_t off = v * 16;
-        const size_t quad = off / (4 * (size_t)K);
-        const size_t rem = off % (4 * (size_t)K);
-        const int c = (int)(rem / 2048);
-        const int wc = min(512, K - c * 512);
-        const int inner = (int)(rem - (size_t)c * 2048);
-        const int r = inner / wc, i = inner % wc;
-        const size_t row = quad * 4 + r;
+        const size_t unit = off / 2048;
+        const int inner = (int)(off % 2048);
+        const size_t T = unit / nkb;
+        const int kb = (int)(unit % nkb);
+        const int r = inner / 128, pos = inner % 128;
+        const int half = (pos / 64) ^ (r & 1), i = pos % 64;
+        const size_t row = T * 16 + r;
         uint4 val = make_uint4(0, 0, 0, 0);
-        if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)c * 512 + i);
+        if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)kb * 128 + half * 64 + i);
         *reinterpret_cast<uint4*>(dst + off) = val;
     }
 }
@@ -295,7 +296,7 @@ static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, 
 }
 
 cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st) {
-    const int rows_pad = (rows + 3) & ~3;
+    const int rows_pad = (rows + 15) & ~15;
     const size_t total16 = (size_t)rows_pad * K / 16;
     tile_weight_kernel<<<1024, 256, 0, st>>>(src, rows, K, dst, total16);
     return cudaGetLastError();

@@ -14,6 +14,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -22,17 +23,22 @@
 #include "qres_common.cuh"
 
 namespace qres {
-cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int epi, void* out, int ld_out,
-                        int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out);
+cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
+                        int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
+                        void* work, size_t work_bytes, int kb0, int kb1, const qres_weight* next, int next_prefetch);
+size_t gemv_workspace_bytes(int grid, int max_tiles);
+int gemv_max_kb(int users);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
-                       uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl);
+                       uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
+                       const void* pf, size_t pf_bytes);
 size_t attn_workspace_bytes(int nranks, int rows, int nchunks);
 int attn_default_chunks(int nranks, int rows, int sm_count, int max_pages);
 cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const int32_t* page_table,
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
-                        void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl);
+                        void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
+                        const void* pf, size_t pf_bytes);
 cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st);
 cudaError_t quantize_fp8_launch(const float* w, int N, int K, uint8_t* q, float* scales, cudaStream_t st);
 int topk_default_blocks(int n);
@@ -129,6 +135,8 @@ struct qres_ctx {
     int attn_chunks = 1;
     void* topk_work = nullptr;
     int topk_blk = 1;
+    void* gemv_work = nullptr;
+    size_t gemv_work_bytes = 0;
     ncclComm_t comm = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -168,8 +176,16 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, xb, partial, y, o, a, argmax, gathered, attn, topk, total;
+    size_t err, xb, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
 };
+
+int max_tiles(const qres_ctx* c) {
+    int rows = kHidden;
+    rows = std::max(rows, 2 * c->ic);
+    rows = std::max(rows, c->ld_y);
+    rows = std::max(rows, c->vocab_local);
+    return (rows + 15) / 16;
+}
 
 Carve carve(const qres_ctx* c) {
     Carve k;
@@ -190,13 +206,15 @@ Carve carve(const qres_ctx* c) {
     k.gathered = take((size_t)c->nranks * R * 2 * QRES_TOPK * 4);
     k.attn = take(attn_workspace_bytes(c->nranks, R, c->attn_chunks));
     k.topk = take(c->vocab_local ? topk_workspace_bytes(R, c->topk_blk) : 0);
+    k.gemv_bytes = gemv_workspace_bytes(2 * c->sm_count, max_tiles(c));
+    k.gemv = take(k.gemv_bytes);
     k.total = off;
     return k;
 }
 
 qres_status check_weight(qres_ctx* c, const qres_weight* w, int rows, int K, const char* what) {
-    if (!w || !w->data || !w->scales || !w->sidx) return fail(c, QRES_ERR_ARG, "%s: null pointer", what);
-    if (w->rows != rows || w->K != K || w->rows_pad != ((rows + 3) & ~3) || w->n_scale_rows < 1)
+    if (!w || !w->data || !w->uscale) return fail(c, QRES_ERR_ARG, "%s: null pointer", what);
+    if (w->rows != rows || w->K != K || w->rows_pad != ((rows + 15) & ~15))
         return fail(c, QRES_ERR_ARG, "%s: shape rows=%d K=%d rows_pad=%d (want rows=%d K=%d)", what, w->rows, w->K,
                     w->rows_pad, rows, K);
     return QRES_OK;
@@ -362,6 +380,8 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->attn_work = w + k.attn;
     c->attn_work_bytes = attn_workspace_bytes(c->nranks, c->cfg.rows, c->attn_chunks);
     c->topk_work = c->vocab_local ? (void*)(w + k.topk) : nullptr;
+    c->gemv_work = w + k.gemv;
+    c->gemv_work_bytes = k.gemv_bytes;
     return QRES_OK;
 }
 
@@ -403,7 +423,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (at ? (!L.wq || !c->cos_tab || !c->io.page_table) : (!L.taps))
             return fail(c, QRES_ERR_STATE, "layer %d: parameters not bound", l);
     }
-    const int grid = c->sm_count;
+    const int grid = 2 * c->sm_count;  // two weight-streaming CTAs per SM
     const int32_t* pos = c->io.tok->pos;
     int launches = 0;
     auto K = [&](cudaError_t e, const char* what) -> qres_status {
@@ -426,20 +446,51 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         return QRES_OK;
     };
     // a GEMV with the rmsnorm prologue over the residual (adding pending partials first when TP)
+    // the weight-streaming projections in step order: each launch prefetches the start of the next one into
+    // L2 once its own stream is done (the lm_head's next is layer 0's in-projection of the following step)
+    std::vector<const qres_weight*> order;
+    for (int l = 0; l < c->cfg.layers; ++l) {
+        const Layer& L = c->layers[l];
+        order.push_back(&L.w[is_attn(c, l) ? QRES_W_ATTN_IN : QRES_W_GDN_IN]);
+        order.push_back(&L.w[QRES_W_OUT]);
+        order.push_back(&L.w[QRES_W_GATEUP]);
+        order.push_back(&L.w[QRES_W_DOWN]);
+    }
+    if (c->cfg.vocab) order.push_back(&c->head);
+    auto next_of = [&](const qres_weight* w) -> const qres_weight* {
+        for (size_t i = 0; i < order.size(); ++i)
+            if (order[i] == w) return order[(i + 1) % order.size()];
+        return nullptr;
+    };
+    const int kPrefetchUnits = 16;  // 32 KB per warp
+    auto gemv = [&](const qres_weight& w, int pro, const void* in, int ld_in, int epi, void* out, int ld_out,
+                    const float* red, float* x_out, int kb0, int kb1, const char* what) -> qres_status {
+        return K(gemv_launch(w, R, pro, in, ld_in, epi, out, ld_out, grid, c->err, st, true, red, x_out, c->gemv_work,
+                             c->gemv_work_bytes, kb0, kb1, next_of(&w), kPrefetchUnits),
+                 what);
+    };
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
         if (pending) {
-            qres_status s = K(gemv_launch(w, R, 2, cur, epi, out, ld_out, grid, c->err, st, true, c->partial, other), what);
+            qres_status s = gemv(w, 2, cur, kHidden, epi, out, ld_out, c->partial, other, 0, 0, what);
             std::swap(cur, other);
             pending = false;
             return s;
         }
-        return K(gemv_launch(w, R, 0, cur, epi, out, ld_out, grid, c->err, st, true, nullptr, nullptr), what);
+        return gemv(w, 0, cur, kHidden, epi, out, ld_out, nullptr, nullptr, 0, 0, what);
     };
+    // a row-parallel projection: residual update (one rank) or fp32 partial + all-reduce (TP). When the rows'
+    // activations exceed shared memory (8 users x K 17408) the K range is covered by several launches, each
+    // adding its part in order.
     auto row_parallel = [&](const qres_weight& w, const uint16_t* in, const char* what) -> qres_status {
-        if (!tp) return K(gemv_launch(w, R, 1, in, 2, cur, kHidden, grid, c->err, st, true, nullptr, nullptr), what);
-        qres_status s = K(gemv_launch(w, R, 1, in, 3, c->partial, kHidden, grid, c->err, st, true, nullptr, nullptr), what);
-        if (s) return s;
-        s = allreduce();
+        const int nkb = w.K / 128, step = gemv_max_kb(R);
+        for (int kb0 = 0; kb0 < nkb; kb0 += step) {
+            const int kb1 = std::min(nkb, kb0 + step);
+            const int epi = !tp ? 2 : (kb0 == 0 ? 3 : 2);
+            qres_status s = gemv(w, 1, in, w.K, epi, tp ? c->partial : cur, kHidden, nullptr, nullptr, kb0, kb1, what);
+            if (s) return s;
+        }
+        if (!tp) return QRES_OK;
+        qres_status s = allreduce();
         pending = true;
         return s;
     };
@@ -449,14 +500,17 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         uint16_t* mcopy = (l == c->cfg.layers - 1) ? c->io.mixer_out : nullptr;
         qres_status s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
         if (s) return s;
+        // the mixer is latency-bound: it pulls the whole out-projection into L2 meanwhile
+        const void* pf = L.w[QRES_W_OUT].data;
+        const size_t pf_bytes = (size_t)L.w[QRES_W_OUT].rows_pad * L.w[QRES_W_OUT].K;
         if (at) {
             STEP(attn_launch(n, R, c->y, c->ld_y, pos, c->io.page_table, c->cfg.max_pages, c->cfg.num_pages, L.wq, L.wk,
                              c->cos_tab, c->sin_tab, c->max_pos, L.st.k_pool, L.st.v_pool, c->o, mcopy, c->attn_work,
-                             c->attn_work_bytes, c->attn_chunks, c->err, st, true),
+                             c->attn_work_bytes, c->attn_chunks, c->err, st, true, pf, pf_bytes),
                  "attention");
         } else {
             STEP(gdn_launch(n, R, c->y, c->ld_y, pos, L.taps, L.dt, L.neg_a, L.norm_w, L.st.gdn_state, L.st.conv_hist,
-                            c->o, mcopy, c->err, st, true),
+                            c->o, mcopy, c->err, st, true, pf, pf_bytes),
                  "gdn");
         }
         s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");
@@ -550,21 +604,44 @@ int32_t qres_step_launches(const qres_ctx* c) { return c ? c->launches : 0; }
 
 // ---- single kernels ----
 
-qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
-                      int32_t grid, uint32_t* err, void* stream) {
-    if (!w || !in || !out || pro < 0 || pro > 1 || epi < 0 || epi > 3)
-        return fail(nullptr, QRES_ERR_ARG, "qres_gemv: bad argument");
-    int sms = 148;
+qres_status qres_gemv_workspace_size(int32_t grid, int32_t rows_pad, size_t* bytes) {
+    if (!bytes || rows_pad < 16) return fail(nullptr, QRES_ERR_ARG, "qres_gemv_workspace_size: bad argument");
     if (grid <= 0) {
         int dev = 0;
         cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        grid = sms;
+        cudaDeviceGetAttribute(&grid, cudaDevAttrMultiProcessorCount, dev);
+        grid *= 2;
+    }
+    *bytes = gemv_workspace_bytes(grid, (rows_pad + 15) / 16);
+    return QRES_OK;
+}
+
+qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
+                      int32_t grid, uint32_t* err, void* work, size_t work_bytes, void* stream) {
+    if (!w || !in || !out || !work || pro < 0 || pro > 1 || epi < 0 || epi > 3)
+        return fail(nullptr, QRES_ERR_ARG, "qres_gemv: bad argument");
+    if (grid <= 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&grid, cudaDevAttrMultiProcessorCount, dev);
+        grid *= 2;  // two CTAs per SM
     }
     const int ld_out = epi == 1 ? w->rows / 2 : w->rows;
-    cudaError_t e = gemv_launch(*w, rows, pro, in, epi, out, ld_out, grid, err, static_cast<cudaStream_t>(stream), false,
-                                nullptr, nullptr);
-    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(e));
+    const int nkb = w->K / 128, step = pro == 1 ? gemv_max_kb(rows) : nkb;
+    if (pro == 0 && nkb > gemv_max_kb(rows)) return fail(nullptr, QRES_ERR_ARG, "qres_gemv: rows x K too large for rmsnorm");
+    for (int kb0 = 0; kb0 < nkb; kb0 += step) {
+        const int kb1 = std::min(nkb, kb0 + step);
+        // a K range after the first accumulates into the output (fp32 epilogues only)
+        int e = epi;
+        if (kb0 > 0) {
+            if (epi != 2 && epi != 3) return fail(nullptr, QRES_ERR_ARG, "qres_gemv: K split needs an fp32 epilogue");
+            e = 2;
+        }
+        cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, e, out, ld_out, grid, err,
+                                     static_cast<cudaStream_t>(stream), false, nullptr, nullptr, work, work_bytes, kb0, kb1,
+                                     nullptr, 0);
+        if (ce != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(ce));
+    }
     return QRES_OK;
 }
 
@@ -574,7 +651,7 @@ qres_status qres_gdn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int3
     if (!y || !pos || !taps || !dt || !neg_a || !norm_w || !state || !conv_hist || !o)
         return fail(nullptr, QRES_ERR_ARG, "qres_gdn_mixer: null argument");
     cudaError_t e = gdn_launch(nranks, rows, y, ld_y, pos, taps, dt, neg_a, norm_w, state, conv_hist, o, nullptr, err,
-                               static_cast<cudaStream_t>(stream), false);
+                               static_cast<cudaStream_t>(stream), false, nullptr, 0);
     if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gdn_mixer: %s", cudaGetErrorString(e));
     return QRES_OK;
 }
@@ -602,7 +679,7 @@ qres_status qres_attn_mixer(int32_t nranks, int32_t rows, const uint16_t* y, int
     // num_pages / max_pos bounds: the caller's pool holds max_pages * rows pages at most in this entry point
     cudaError_t e = attn_launch(nranks, rows, y, ld_y, pos, page_table, max_pages, max_pages * rows, wq, wk, cos_tab,
                                 sin_tab, max_pages * kKvBlock, k_pool, v_pool, o, nullptr, work, work_bytes, chunks, err,
-                                static_cast<cudaStream_t>(stream), false);
+                                static_cast<cudaStream_t>(stream), false, nullptr, 0);
     if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_attn_mixer: %s", cudaGetErrorString(e));
     return QRES_OK;
 }

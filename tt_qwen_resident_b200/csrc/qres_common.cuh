@@ -127,6 +127,33 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// global -> shared bulk copy with an L2 cache policy (e.g. evict_first for data read exactly once)
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// L2 prefetch of [p, p + bytes) spread over `n` participants (participant i takes its share), 16-byte granules
+__device__ __forceinline__ void l2_prefetch_share(const uint8_t* p, size_t bytes, int i, int n) {
+    const size_t per = ((bytes + n - 1) / n + 15) & ~size_t(15);
+    size_t a = (size_t)i * per;
+    if (a >= bytes) return;
+    size_t e = a + per < bytes ? a + per : bytes;
+    for (; a < e; a += 65536) {
+        const size_t len = (e - a) < 65536 ? (e - a) : 65536;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + a), "r"((uint32_t)((len + 15) & ~size_t(15))) : "memory");
+    }
+}
+
 // L2 prefetch of a global range (no shared destination)
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

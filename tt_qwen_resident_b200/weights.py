@@ -11,7 +11,8 @@ Canonical layout (projection weights [out_features, in_features], FP8-e4m3 + one
   attn in-proj [14336, 5120]  rows q(24x256) | gate(24x256) | k(4x256) | v(4x256)
   out-proj [5120, 6144], gate / up [17408, 5120], down [5120, 17408], lm_head [vocab, 5120]
 A rank's projection keeps the canonical quantisation: its rows (and K range) are gathered, every row keeps
-the scale row of its 128-row block (``sidx``), and the bytes are re-laid into the GEMV's quad/chunk layout.
+the scale of its 128-row block (streamed per 16 x 128 unit, ``uscale``), and the bytes are re-laid into the
+GEMV's tile/unit layout.
 """
 import ctypes
 import math
@@ -47,25 +48,16 @@ class GemvWeight:
     """one rank's projection in the GEMV layout (device tensors)"""
 
     data: torch.Tensor  # uint8 [rows_pad * K]
-    scales: torch.Tensor  # fp32 [n_scale_rows, K / 128]
-    sidx: torch.Tensor  # int32 [rows_pad]
+    uscale: torch.Tensor  # fp32 [rows_pad / 16, K / 128, 2]: per 16-row x 128-K unit, the scale of rows r % 4 < 2, >= 2
     rows: int
     K: int
 
     @property
     def rows_pad(self):
-        return (self.rows + 3) // 4 * 4
+        return (self.rows + 15) // 16 * 16
 
     def cstruct(self):
-        return _lib.Weight(
-            self.data.data_ptr(),
-            self.scales.data_ptr(),
-            self.sidx.data_ptr(),
-            self.rows,
-            self.rows_pad,
-            self.K,
-            self.scales.shape[0],
-        )
+        return _lib.Weight(self.data.data_ptr(), self.uscale.data_ptr(), self.rows, self.rows_pad, self.K, 0)
 
     @property
     def nbytes(self):
@@ -140,7 +132,9 @@ def quantize(w):
 
 
 def shard(m, rows=None, k=None, device="cuda"):
-    """rank projection of canonical m: rows (LongTensor of canonical rows; None = all), k = (k0, k1) K range"""
+    """rank projection of canonical m: rows (LongTensor of canonical rows; None = all), k = (k0, k1) K range.
+    Every 16-row tile may hold rows of at most two 128-row scale blocks, split by r % 4 < 2 / >= 2 (true for the
+    shards of this model: head / column ranges are 16-aligned, gate|up interleaves pairs)."""
     q, sc = m.q, m.scales
     N, K = q.shape
     rows = torch.arange(N) if rows is None else rows
@@ -148,15 +142,20 @@ def shard(m, rows=None, k=None, device="cuda"):
     assert k0 % 128 == 0 and k1 % 128 == 0
     rows_d = rows.to(q.device)
     ql = q.index_select(0, rows_d)[:, k0:k1].contiguous().to(device)
-    blk = rows // 128  # canonical scale row of every local row
-    used, sidx = torch.unique(blk, sorted=True, return_inverse=True)
-    scales = sc[used.to(sc.device)][:, k0 // 128 : k1 // 128].contiguous().to(device, torch.float32)
-    rows_pad = (len(rows) + 3) // 4 * 4
-    sidx_p = torch.zeros(rows_pad, dtype=torch.int32)
-    sidx_p[: len(rows)] = sidx.to(torch.int32)
-    sidx_p[len(rows) :] = sidx[-1].to(torch.int32)
+    n = len(rows)
+    rows_pad = (n + 15) // 16 * 16
+    blk = torch.empty(rows_pad, dtype=torch.long)
+    blk[:n] = rows // 128  # canonical scale row of every local row
+    blk[n:] = blk[n - 1]
+    tb = blk.view(-1, 4, 4)  # [tiles, quad, row in quad]
+    sa, sb = tb[:, :, :2].reshape(-1, 8), tb[:, :, 2:].reshape(-1, 8)
+    if not (bool((sa == sa[:, :1]).all()) and bool((sb == sb[:, :1]).all())):
+        raise ValueError("a 16-row tile mixes more than two scale blocks")
+    kb0, kb1 = k0 // 128, k1 // 128
+    scd = sc.to(device, torch.float32)
+    us = torch.stack([scd[sa[:, 0].to(device)][:, kb0:kb1], scd[sb[:, 0].to(device)][:, kb0:kb1]], dim=-1)
     data = _lib.tile_weight(ql)
-    return GemvWeight(data=data, scales=scales, sidx=sidx_p.to(device), rows=len(rows), K=k1 - k0)
+    return GemvWeight(data=data, uscale=us.contiguous(), rows=n, K=k1 - k0)
 
 
 def stack_matrices(a, b):
