@@ -184,6 +184,18 @@ QRES_API qres_status qres_topk_workspace_size(int32_t rows, int32_t n_logits, si
 QRES_API qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base, uint32_t* lists,
                       int32_t* argmax, void* work, size_t work_bytes, void* stream);
 
+/* The same top-32 / argmax as qres_topk without a workspace argument: it allocates nothing. It has no
+ * counterpart in the reference. It is for callers that cannot allocate device memory -- a host framework that
+ * owns every device byte through its own pool and hands a plugin only its inputs and outputs. Its scratch (the
+ * per-block candidate lists and per-row tickets) is a fixed 256 KiB device array inside the library, held by
+ * every GPU that loads it until exit; requests larger than that (more than 8 rows of 260,096 logits) are
+ * rejected with QRES_ERR_ARG. The first call on a device looks up the array's device address with
+ * cudaGetSymbolAddress (make that first call before any stream capture). All calls share the array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be serialised by the caller. Each call clears
+ * the tickets it needs before its kernel. */
+QRES_API qres_status qres_topk_noalloc(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base,
+                                       uint32_t* lists, int32_t* argmax, void* stream);
+
 /* ---- weight preparation ---- */
 /* fp32 [N][K] -> e4m3 bytes [N][K] + scales [ceil(N/128)][K/128] (amax / 448 per 128 x 128 block). */
 QRES_API qres_status qres_quantize_fp8(const float* w, int32_t N, int32_t K, uint8_t* q, float* scales, void* stream);

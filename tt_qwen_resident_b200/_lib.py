@@ -46,6 +46,7 @@ EXPORTS = [
     "qres_attn_mixer",
     "qres_topk_workspace_size",
     "qres_topk",
+    "qres_topk_noalloc",
     "qres_quantize_fp8",
     "qres_tile_weight",
 ]
@@ -142,6 +143,7 @@ def lib():
             "qres_attn_mixer": [i32, i32, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp],
             "qres_topk_workspace_size": [i32, i32, ctypes.POINTER(sz)],
             "qres_topk": [i32, vp, i32, i32, vp, vp, vp, sz, vp],
+            "qres_topk_noalloc": [i32, vp, i32, i32, vp, vp, vp],
             "qres_quantize_fp8": [vp, i32, i32, vp, vp, vp],
             "qres_tile_weight": [vp, i32, i32, vp, vp],
         }

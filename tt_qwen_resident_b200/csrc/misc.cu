@@ -5,6 +5,8 @@
 //    reference's sampling.hpp (:24-74): bf16 order keys descending, the smaller vocab index first on ties;
 //  - embed_rows: the step's input rows, x0 or embed[token] (streamer_reader.cpp:117-128);
 //  - feed: the device-fed next token state (mlp_hub.cpp:414-458): token = greedy pick, pos + 1.
+#include <mutex>
+
 #include "qres_common.cuh"
 
 namespace qres {
@@ -393,5 +395,45 @@ cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(256), 0, st, at, pdl);
     return cudaLaunchKernelEx(&cfg, merge_lists_kernel, lists, nlists, rows, out, argmax);
 }
+
+}  // namespace qres
+
+namespace qres {
+
+// ------------------------------------------------------------------------------------------------ top-k, no allocation
+// The top-k of qres_topk_noalloc keeps its scratch (the per-block candidate lists and the per-row tickets) in this
+// fixed device array instead of a caller-provided workspace. It is sized for 8 rows of the full 248,320-entry
+// vocabulary (8 x 122 blocks of 256 bytes, plus the tickets): 256 KiB, held by every GPU that loads the library
+// until the process exits. All calls share it and it keeps the last call's contents.
+constexpr size_t kTopkStaticScratch = 256 * 1024;
+static __device__ __align__(256) uint8_t g_topk_scratch[kTopkStaticScratch];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_topk_scratch_mu;
+void* g_topk_scratch_ptr[kMaxDevices] = {};  // device address of g_topk_scratch, per device
+}  // namespace
+
+// the device address of the scratch array on the current device (looked up once per device; the host-side name
+// g_topk_scratch is only a stand-in and must never be passed to a kernel)
+cudaError_t topk_static_scratch(void** out, size_t* bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_topk_scratch_mu);
+    if (g_topk_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_topk_scratch);
+        if (e != cudaSuccess) return e;
+        g_topk_scratch_ptr[dev] = p;
+    }
+    *out = g_topk_scratch_ptr[dev];
+    *bytes = kTopkStaticScratch;
+    return cudaSuccess;
+}
+
+// byte offset of the per-row tickets inside a top-k workspace (they must start every call at zero)
+size_t topk_ticket_offset(int rows, int nblk) { return (size_t)rows * nblk * 2 * kTopK * 4 + 256; }
 
 }  // namespace qres

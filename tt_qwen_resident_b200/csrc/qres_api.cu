@@ -47,6 +47,8 @@ cudaError_t topk_launch(int rows, const uint16_t* logits, int n, int ld, int bas
                         void* work, int nblk, cudaStream_t st, bool pdl);
 cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint32_t* out, int32_t* argmax,
                                cudaStream_t st, bool pdl);
+cudaError_t topk_static_scratch(void** out, size_t* bytes);
+size_t topk_ticket_offset(int rows, int nblk);
 cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x, int rows,
                               uint32_t* err, cudaStream_t st, bool pdl);
 cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl);
@@ -698,6 +700,31 @@ qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, in
     cudaError_t e = topk_launch(rows, logits, n_logits, n_logits, base, lists, argmax, work, nblk,
                                 static_cast<cudaStream_t>(stream), false);
     if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_topk: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_topk_noalloc(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base, uint32_t* lists,
+                              int32_t* argmax, void* stream) {
+    if (!logits || !lists || rows < 1 || rows > QRES_MAX_ROWS || n_logits < 1)
+        return fail(nullptr, QRES_ERR_ARG, "qres_topk_noalloc: bad argument");
+    const int nblk = topk_default_blocks(n_logits);
+    void* scratch = nullptr;
+    size_t cap = 0;
+    cudaError_t e = topk_static_scratch(&scratch, &cap);
+    if (e != cudaSuccess)
+        return fail(nullptr, QRES_ERR_CUDA, "qres_topk_noalloc: scratch address: %s", cudaGetErrorString(e));
+    const size_t need = topk_workspace_bytes(rows, nblk);
+    if (need > cap)
+        return fail(nullptr, QRES_ERR_ARG,
+                    "qres_topk_noalloc: %d rows x %d logits need %zu bytes of scratch, the fixed array holds %zu "
+                    "(at most 8 rows of 260,096 logits); use qres_topk with a workspace",
+                    rows, n_logits, need, cap);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the tickets must start at zero: a call that stopped early (an error) may have left them set
+    e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + topk_ticket_offset(rows, nblk), 0, (size_t)rows * 4, st);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_topk_noalloc: %s", cudaGetErrorString(e));
+    e = topk_launch(rows, logits, n_logits, n_logits, base, lists, argmax, scratch, nblk, st, false);
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_topk_noalloc: %s", cudaGetErrorString(e));
     return QRES_OK;
 }
 
