@@ -64,15 +64,16 @@ typedef struct {
 } qres_config;
 
 /* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block of the canonical matrix), in the
- * GEMV layout made by qres_tile_weight: rows in tiles of 16 (zero-padded), a tile's K in 128-wide units of 2 KB
- * stored back to back, inside a unit row r at r * 128 with its two 64-byte halves swapped when r is odd.
- * uscale gives every unit its block scales: .x for the unit's rows with r % 4 < 2, .y for r % 4 >= 2 (the two
- * halves of a gate|up quad; equal elsewhere). */
+ * GEMV layout made by qres_tile_weight: rows in tiles of 128 (zero-padded), a tile's K in 128-wide units of
+ * 16 KB stored back to back, inside a unit the tensor core's no-swizzle K-major core matrices (byte (r, c) at
+ * (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16). uscale points at the scale table: per tile, 128
+ * bytes of row selectors (row r's canonical 128-row block is the tile's slot sel[r], 0..7), then for each
+ * 128-K block the 8 slots' fp32 scales -- (128 + (K / 128) * 32) bytes per tile. */
 typedef struct {
     const void* data;      /* rows_pad * K bytes */
-    const float* uscale;   /* [rows_pad / 16][K / 128][2] */
+    const float* uscale;   /* the scale table, rows_pad / 128 tiles */
     int32_t rows;          /* real rows */
-    int32_t rows_pad;      /* rows rounded up to a multiple of 16 */
+    int32_t rows_pad;      /* rows rounded up to a multiple of 128 (at most 524,288) */
     int32_t K;             /* multiple of 128 */
     int32_t reserved;
 } qres_weight;
@@ -159,8 +160,10 @@ QRES_API int32_t qres_step_launches(const qres_ctx* ctx);
 /* ---- single kernels (the building blocks of a step, for tests and microbenchmarks) ---- */
 /* y = act(h @ W^T) for `rows` users: pro 0 = h = bf16(rmsnorm(x)) from fp32 x [rows][K]; pro 1 = h = bf16
  * input [rows][K]. epi 0 = bf16 out [rows][w.rows]; 1 = SwiGLU over interleaved gate|up pairs, bf16 out
- * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid 0 = twice the SM count.
- * work: qres_gemv_workspace_size bytes (split-tile partials and tickets), zeroed once before first use. */
+ * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid: CTAs requested (0 = twice
+ * the SM count; fewer are launched when the weight has fewer 128 x 128 units). work: qres_gemv_workspace_size
+ * bytes for that grid (split-tile tickets and partials), zeroed once before first use (every launch leaves it
+ * reusable). */
 QRES_API qres_status qres_gemv_workspace_size(int32_t grid, int32_t rows_pad, size_t* bytes);
 QRES_API qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
                       int32_t grid, uint32_t* err, void* work, size_t work_bytes, void* stream);
@@ -199,7 +202,7 @@ QRES_API qres_status qres_topk_noalloc(int32_t rows, const uint16_t* logits, int
 /* ---- weight preparation ---- */
 /* fp32 [N][K] -> e4m3 bytes [N][K] + scales [ceil(N/128)][K/128] (amax / 448 per 128 x 128 block). */
 QRES_API qres_status qres_quantize_fp8(const float* w, int32_t N, int32_t K, uint8_t* q, float* scales, void* stream);
-/* row-major e4m3 [rows][K] -> the GEMV layout of qres_weight (rows_pad = rows rounded up to 16, zero rows). */
+/* row-major e4m3 [rows][K] -> the GEMV layout of qres_weight (rows_pad = rows rounded up to 128, zero rows). */
 QRES_API qres_status qres_tile_weight(const uint8_t* src, int32_t rows, int32_t K, uint8_t* dst, void* stream);
 
 #ifdef __cplusplus

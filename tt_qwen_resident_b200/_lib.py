@@ -217,9 +217,9 @@ def quantize_fp8(w, stream=None):
 
 
 def tile_weight(q, stream=None):
-    """row-major e4m3 [rows][K] (device) -> the GEMV layout (rows padded to a multiple of 16)"""
+    """row-major e4m3 [rows][K] (device) -> the GEMV layout (rows padded to a multiple of 128)"""
     rows, K = q.shape
-    rows_pad = (rows + 15) // 16 * 16
+    rows_pad = (rows + 127) // 128 * 128
     dst = torch.empty(rows_pad * K, dtype=torch.uint8, device=q.device)
     check(lib().qres_tile_weight(ptr(q.contiguous()), rows, K, ptr(dst), stream_ptr(stream)), None, "tile")
     return dst

@@ -1,34 +1,39 @@
-// Block-scaled FP8 weight-streaming projection for 1..8 rows (users) on sm_100a tensor cores.
+// Block-scaled FP8 weight-streaming projection for 1..8 rows (users) on the sm_100a tensor cores (tcgen05).
 //
 // Replaces the reference's streamer cores (qwen36_resident/kernels/streamer_reader.cpp:45-89 weight ring,
 // streamer_compute.cpp:60-92 M=1..8 matmul, :100-210 rmsnorm, :212-249 silu(g)*u, :252-273 residual fold).
 //
-// Math: out[u][n] = sum_kb scale[sidx[n]][kb] * sum_{k in kb} h[u][k] * q[n][k], q the e4m3 weight, h the bf16
-// activation; every product is exact (e4m3 -> f16 and bf16 -> f16 are exact conversions in the f16 range,
-// f16 x f16 fits fp32) and accumulates in fp32. Each 16-row x 128-K block is one mma.sync.m16n8k16 chain of 8
-// MMAs (weights as A, the rows' activations as B: one user per column, so 8 users cost what one does), then
-// scaled by its block scale into the fp32 result.
+// Math: out[u][n] = sum_kb scale[n][kb] * sum_{k in kb} q[n][k] * h[u][k], q the e4m3 weight, h the bf16
+// activation, scale the fp32 scale of the 128 x 128 block holding (n, kb). Each 128-row x 128-K block ("unit")
+// is one chain of 4 tcgen05.mma.kind::f8f6f4 (M = 128, N = 16, K = 32) with the weights as A, read by the tensor
+// core straight from the shared-memory stage the bulk copy filled, and the activations as B. The activations
+// enter as two e4m3 columns per user: with E the exponent of max|h| over the user's 128-K block, h * 2^(7-E) =
+// hi + lo, hi = e4m3(h * 2^(7-E)), lo = e4m3(h * 2^(7-E) - hi). A bf16 carries 8 significant bits and each
+// e4m3 term 4, so the split is exact for every element within 2^-10 of the block maximum; below that lo is
+// rounded on the e4m3 subnormal grid, an absolute error of at most 2^-18 of the block maximum (far below the
+// bf16 rounding of the result). The products accumulate in fp32 in tensor memory (TMEM); the epilogue warps
+// read each unit's 16 x 128 accumulator, add hi + lo, and fold it into the row's fp32 result with the unit's
+// weight scale times 2^(E-7).
 //
-// Layout (qres_tile_weight): rows in tiles of 16 (zero-padded); a tile's K in 128-wide blocks ("units", 2 KB
-// each, a tile's units back to back); inside a unit row r's 128 bytes at r*128, its two 64-byte halves swapped
-// when r is odd (conflict-free shared-memory reads). One fp32 scale per 128 x 128 block of the canonical
-// matrix; the scales are streamed per unit (uscale: the scale of the unit's rows r % 4 < 2 and r % 4 >= 2,
-// which is all a 16-row tile of these shards ever holds), loaded one stage ahead.
+// Layout (qres_tile_weight): rows in tiles of 128 (zero-padded), a tile's K in 128-wide units of 16 KB stored
+// back to back; inside a unit the canonical no-swizzle K-major arrangement of the tensor core: byte (r, c) at
+// (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16, i.e. 8-row x 16-byte core matrices, K-adjacent ones
+// 128 bytes apart (leading offset), row-adjacent ones 1024 bytes apart (stride offset). The scale table gives
+// each tile 128 bytes of row selectors (which of the tile's <= 8 canonical 128-row blocks holds the row) and
+// 8 fp32 scales per unit (the blocks' scales at that K block).
 //
-// Work split: the tiles x blocks units are divided evenly over every warp of the grid (148 CTAs x 8 warps);
-// each warp streams its contiguous run of units through its own ring of shared-memory stages with
-// cp.async.bulk (no multicast; its first stages are issued before griddepcontrol.wait, so under programmatic
-// dependent launch the weight stream starts while the previous kernel finishes). A warp accumulates a tile in
-// registers; a tile split between warps is finished by the last of them (an atomic ticket), which adds the
-// parts in warp order (deterministic).
-//
-// MMA operand mapping: the 16 k-slots of an MMA may map to any 16 K positions as long as A and B agree. Lane
-// (g, t) (g = lane / 4, t = lane % 4) takes the 4 bytes at K = 64*half + 16*t + 4*m of rows g and g + 8 for MMA
-// m of a half-block. Words m = 0, 1 go through the conversion unit (bytes 0,1 -> k-slots 2t,2t+1; bytes 2,3 ->
-// 2t+8,2t+9); words m = 2, 3 through integer ops (bytes 1,3 -> 2t,2t+1; bytes 0,2 -> 2t+8,2t+9, values scaled
-// by 2^-8, undone once per block), which splits the conversion work between the XU and ALU pipes. The B
-// fragment takes the same positions of user g's h, stored in shared memory in that order (h_slot). Each word m
-// accumulates in its own fragment (short MMA dependency chains).
+// CTA roles (256 threads, one CTA per SM, a second co-resident under programmatic dependent launch):
+//   warp 0 lane 0   streams the CTA's contiguous run of units through a ring of 16 KB stages (cp.async.bulk,
+//                   no multicast; the first stages before griddepcontrol.wait -- weights are immutable);
+//   warp 1          owns the TMEM allocation; lane 0 issues the MMAs of a unit once its stage has landed and
+//                   commits them to the stage's "empty" barrier and to the accumulator slot's "full" barrier;
+//   warps 4..7      (TMEM lanes 0..127, one row each) drain accumulator slots, apply the scales, and finish
+//                   tiles: a tile split between CTAs is completed by the last of them (an atomic ticket), which
+//                   adds the parts in CTA order (deterministic);
+//   all 8 warps     build the activations' hi / lo operand in shared memory first (rmsnorm or a bf16 input).
+// Every wait is bounded (sets the error word and stops the pipeline).
+#include <algorithm>
+
 #include "qres_common.cuh"
 
 namespace qres {
@@ -36,19 +41,24 @@ namespace qres {
 enum { PRO_RMSNORM = 0, PRO_BF16 = 1, PRO_RMSNORM_ADD = 2 };
 enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3 };
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kUnitBytes = 2048;  // 16 rows x 128 K
-constexpr int kStageUnits = 2;
-constexpr int kStageBytes = kStageUnits * kUnitBytes;
-constexpr int kMaxStages = 4;     // per warp
-constexpr int kHPad = 8;          // f16 elements of padding per h row (bank spread between users)
+constexpr int kGemvThreads = 256;
+constexpr int kTileRows = 128;
+constexpr int kUnitBytes = 128 * 128;  // one 128-row x 128-K block of e4m3
+constexpr int kActKb = 1024;           // one user group's operand per 128-K block: 8 columns x 128 bytes
+constexpr int kDSlots = 4;             // TMEM accumulator slots, 16 fp32 columns each
+constexpr int kTmemCols = 64;
+constexpr int kMaxStages = 8;
+constexpr int kSelBytes = 128;         // per tile: the selector of each row
+constexpr int kHeadBytes = 1024;       // barriers and small shared state
+
+// instruction descriptor of tcgen05.mma.kind::f8f6f4: D fp32 (bits 4-5 = 1), A and B e4m3 (bits 7-9, 10-12 =
+// 0), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28
+constexpr uint32_t kIdesc = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
 
 struct GemvParams {
     const uint8_t* w;
-    const float2* uscale;   // [tiles][nkb]: the block scale of each unit's rows r % 4 < 2 (.x) and r % 4 >= 2 (.y)
+    const uint8_t* table;   // per tile: kSelBytes row selectors, then nkb x 8 fp32 scales
     int rows, tiles, K, nkb;
-    int kb0, kb1;           // K blocks [kb0, kb1) of this launch (a K-split launch covers part of K)
     int users;              // real users (<= template B)
     const float* x;         // PRO_RMSNORM(_ADD): fp32 [users][K]
     const float* red;       // PRO_RMSNORM_ADD: all-reduced partials [users][K]; x_out = x + red
@@ -57,62 +67,126 @@ struct GemvParams {
     int ld_in;
     void* out;              // EPI_BF16 / EPI_SILU_MUL: bf16 [users][ld_out]; EPI_RESID / EPI_F32: fp32
     int ld_out;
-    int nstages;            // ring depth per warp
-    float* part;            // [grid * 8 warps][2][128]: a warp's split first / last tile
+    int nstages;            // ring depth
+    int nkw;                // K blocks in this CTA's activation window (the most any CTA needs)
+    float* part;            // [grid][2][8][128]: a CTA's split first / last tile
     int* ticket;            // [tiles]
-    // the next weight-streaming projection of the step (same grid): once its own stream is done, every warp
-    // prefetches the start of its range there into L2, so HBM keeps streaming through this kernel's tail
-    const uint8_t* next_w;
-    int next_units;         // units of the next launch
-    int next_prefetch;      // units per warp to prefetch
+    const uint8_t* next_w;  // the next projection of the step: the start of this CTA's range is pulled into L2
+    int next_units;
+    int next_prefetch;      // units per CTA
     uint32_t* err;
 };
 
-__host__ __device__ inline size_t gemv_h_bytes(int B, int K) { return ((size_t)B * (K + kHPad) * 2 + 127) & ~size_t(127); }
-
-__host__ __device__ inline size_t gemv_smem_bytes(int B, int K, int nstages) {
-    return 512 /* barriers */ + gemv_h_bytes(B, K) + (size_t)kGemvWarps * nstages * kStageBytes;
+__host__ __device__ inline size_t gemv_act_bytes(int B, int nkw) { return (size_t)(B > 4 ? 2 : 1) * nkw * kActKb; }
+__host__ __device__ inline size_t gemv_ainv_bytes(int nkw) { return ((size_t)nkw * 8 * 4 + 127) & ~size_t(127); }
+__host__ __device__ inline size_t gemv_smem_bytes(int B, int nkw, int nstages) {
+    const size_t pre = kHeadBytes + gemv_ainv_bytes(nkw) + gemv_act_bytes(B, nkw);
+    return ((pre + 1023) & ~size_t(1023)) + (size_t)nstages * kUnitBytes;
 }
 
-// 4 e4m3 bytes (K positions P..P+3) -> two f16x2 by the conversion unit: lo = (P, P+1), hi = (P+2, P+3), exact
-__device__ __forceinline__ void cvt_word_xu(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
-        : "=r"(lo), "=r"(hi)
-        : "r"(w));
+// ---- tcgen05 wrappers (cta_group::1) ------------------------------------------------------------------------
+
+// shared-memory matrix descriptor, no swizzle: start, leading (K) and stride (M/N) byte offsets, version 1
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 
-// the same 4 bytes by integer ops, each as the f16 with bits (s << 15) | (low7 << 7): the e4m3 value times 2^-8,
-// exact for normals and subnormals alike. odd = (P+1, P+3), even = (P, P+2) -- a different pairing, matched by
-// the activations' layout in shared memory.
-__device__ __forceinline__ void cvt_word_alu(uint32_t w, uint32_t& odd, uint32_t& even) {
-    odd = (w & 0x80008000u) | ((w >> 1) & 0x3F803F80u);
-    const uint32_t w8 = w << 8;
-    even = (w8 & 0x80008000u) | ((w8 >> 1) & 0x3F803F80u);
-}
-
-// position of K index k of the activations in shared memory: inside every 16-group, the second 8 positions
-// (the words converted by cvt_word_alu) are stored per 4-group as (1, 3, 0, 2)
-__device__ __forceinline__ int h_slot(int k) {
-    const int r = k & 15;
-    if (r < 8) return k;
-    const int q = r & 3;
-    const int to = (q == 0) ? 2 : (q == 1) ? 0 : (q == 2) ? 3 : 1;
-    return (k & ~3) + to;
-}
-
-__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
+__device__ __forceinline__ void tc_mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(accumulate), "r"(kIdesc)
+        : "memory");
+}
+
+// arrive on `bar` once every tcgen05 operation this thread issued so far has completed
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// whole warp: allocate `cols` TMEM columns, base address written to *dst (shared memory)
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols) : "memory");
+}
+
+// this warp's 32 TMEM lanes x NC consecutive fp32 columns (one lane per thread); the load and its wait are one
+// statement, so no use of the values can be scheduled before the wait
+template <int NC>
+__device__ __forceinline__ void tmem_load(uint32_t taddr, float* v);
+
+template <>
+__device__ __forceinline__ void tmem_load<2>(uint32_t a, float* v) {
+    uint32_t r0, r1;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];\n\ttcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(a)
+                 : "memory");
+    v[0] = __uint_as_float(r0);
+    v[1] = __uint_as_float(r1);
+}
+template <>
+__device__ __forceinline__ void tmem_load<4>(uint32_t a, float* v) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\ttcgen05.wait::ld.sync.aligned;"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_load<8>(uint32_t a, float* v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(a)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_load<16>(uint32_t a, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];\n\ttcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(a)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// global warp owning unit u when U units are split over W warps (base = U / W, rem = U % W)
-__device__ __forceinline__ int warp_of_unit(int u, int base, int rem) {
+// two floats -> two e4m3 bytes (round to nearest even, saturating), a in the low byte
+__device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+    return r;
+}
+// two e4m3 bytes -> floats (exact)
+__device__ __forceinline__ float2 e4m3x2_f32(uint32_t v) {
+    uint32_t h2;
+    asm("{\n\t.reg .b16 l;\n\tcvt.u16.u32 l, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\t}" : "=r"(h2) : "r"(v));
+    return __half22float2(*reinterpret_cast<__half2*>(&h2));
+}
+
+// CTA owning unit u when U units are split over G CTAs (base = U / G, rem = U % G)
+__device__ __forceinline__ int cta_of_unit(int u, int base, int rem) {
     const int big = rem * (base + 1);
     if (u < big) return u / (base + 1);
     return rem + (u - big) / base;
@@ -120,61 +194,68 @@ __device__ __forceinline__ int warp_of_unit(int u, int base, int rem) {
 
 template <int B, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [8 warps][kMaxStages]
-    __half* hs = reinterpret_cast<__half*>(smem + 512);
-    const int hld = p.K + kHPad;
-    uint8_t* ring = smem + 512 + gemv_h_bytes(B, p.K);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kMaxStages] stage landed
+    uint64_t* empty = full + kMaxStages;                 // [kMaxStages] stage consumed by its MMAs
+    uint64_t* dfull = empty + kMaxStages;                // [kDSlots] accumulator slot written
+    uint64_t* dempty = dfull + kDSlots;                  // [kDSlots] accumulator slot read (4 epilogue warps)
+    uint64_t* drain = dempty + kDSlots;                  // every MMA of the CTA completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    int* tk_slot = reinterpret_cast<int*>(tmem_slot + 1);
+    float (*red)[8] = reinterpret_cast<float (*)[8]>(smem + 512);  // [8 warps][8 users]
+    const int nkw = p.nkw;
+    float* ainv = reinterpret_cast<float*>(smem + kHeadBytes);  // [nkw][8]: 2^(E-7) per K block and user
+    uint8_t* act = smem + kHeadBytes + gemv_ainv_bytes(nkw);   // [group][nkw][8 chunks][8 columns][16 bytes]
+    const size_t pre = kHeadBytes + gemv_ainv_bytes(nkw) + gemv_act_bytes(B, nkw);
+    uint8_t* ring = smem + ((pre + 1023) & ~size_t(1023));
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int K = p.K;
-    const int nkbl = p.kb1 - p.kb0;  // blocks per tile in this launch
-    const int U = p.tiles * nkbl;
-    const int W = gridDim.x * kGemvWarps;
-    const int gw = blockIdx.x * kGemvWarps + warp;
-    const int base = U / W, rem = U % W;
-    const int u0 = gw * base + min(gw, rem);
-    const int cnt = base + (gw < rem ? 1 : 0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = p.K, nkb = p.nkb;
+    const int U = p.tiles * nkb;
+    const int G = gridDim.x;
+    const int base = U / G, rem = U % G;
+    const int u0 = blockIdx.x * base + min((int)blockIdx.x, rem);
+    const int cnt = base + ((int)blockIdx.x < rem ? 1 : 0);
     const int NS = p.nstages;
-    const int nst = (cnt + kStageUnits - 1) / kStageUnits;
-    uint64_t* bars = full + warp * kMaxStages;
-    uint8_t* wring = ring + (size_t)warp * NS * kStageBytes;
+    if (cnt == 0) return;
+    const int kb_start = u0 % nkb;
+    const int nwin = min(cnt, nkb);  // K blocks this CTA touches: a cyclic run starting at kb_start
 
-    if (lane == 0) {
-        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < kDSlots; ++i) {
+            mbar_init(&dfull[i], 1);
+            mbar_init(&dempty[i], 4);
+        }
+        mbar_init(drain, 1);
         fence_mbar_init();
     }
-    __syncwarp();
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
     pdl_launch();
 
-    // stage s of this warp: units [u0 + 2s, min(u0 + 2s + 2, u0 + cnt)); a launch's units of one tile are
-    // contiguous in memory, a stage crossing a tile boundary takes two copies
-    auto unit_addr = [&](int u) -> const uint8_t* {
-        const int T = u / nkbl, kb = p.kb0 + u % nkbl;
-        return p.w + ((size_t)T * p.nkb + kb) * kUnitBytes;
-    };
     const uint64_t pol = policy_evict_first();  // every weight byte is read once per step
-    auto issue = [&](int s) {
-        const int a = u0 + s * kStageUnits, n = min(kStageUnits, u0 + cnt - a);
-        uint8_t* dst = wring + (size_t)(s % NS) * kStageBytes;
-        mbar_arrive_expect_tx(&bars[s % NS], n * kUnitBytes);
-        int i = 0;
-        while (i < n) {
-            int run = 1;
-            while (i + run < n && (a + i + run) % nkbl != 0) ++run;
-            bulk_g2s_hint(dst + i * kUnitBytes, unit_addr(a + i), run * kUnitBytes, &bars[s % NS], pol);
-            i += run;
-        }
+    auto issue = [&](int i) {
+        const int slot = i % NS;
+        mbar_arrive_expect_tx(&full[slot], kUnitBytes);
+        bulk_g2s_hint(ring + (size_t)slot * kUnitBytes, p.w + (size_t)(u0 + i) * kUnitBytes, kUnitBytes, &full[slot], pol);
     };
-    if (lane == 0)
-        for (int s = 0; s < min(NS, nst); ++s) issue(s);
+    if (tid == 0)
+        for (int i = 0; i < min(NS, cnt); ++i) issue(i);
 
     pdl_wait();
     const int users = p.users;
-    // ---- prologue: h (f16 [B][K + pad]) in shared memory, from x (rmsnorm) or a bf16 input
+
+    // ---- prologue: the activations' hi / lo operand for the K blocks of this CTA's window
+    for (int i = tid; i < (int)(gemv_act_bytes(B, nkw) / 16); i += kGemvThreads)
+        reinterpret_cast<uint4*>(act)[i] = make_uint4(0, 0, 0, 0);
+    float rn[B];
     if (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) {
-        __shared__ float red[kGemvWarps][B];
         auto xload = [&](int b, int i) -> float4 {
             float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
             if (PRO == PRO_RMSNORM_ADD) {
@@ -190,7 +271,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         for (int b = 0; b < B; ++b) {
             float ss = 0.f;
             if (b < users) {
-                for (int i = threadIdx.x; i < K / 4; i += kGemvThreads) {
+                for (int i = tid; i < K / 4; i += kGemvThreads) {
                     const float4 v = xload(b, i);
                     if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
                     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -204,236 +285,240 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         for (int b = 0; b < B; ++b) {
             float tsum = 0.f;
 #pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) tsum += red[w][b];
-            const float r = rsqrt_ieee(tsum / (float)K + kEps);
-            __half* hv = hs + (size_t)b * hld;
-            for (int i = threadIdx.x; i < K / 4; i += kGemvThreads) {
-                float4 v = b < users ? xload(b, i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                // h = bf16(x * r), held exactly as f16, at its permuted slot
-                hv[h_slot(4 * i)] = __float2half_rn(bf16_round(v.x * r));
-                hv[h_slot(4 * i + 1)] = __float2half_rn(bf16_round(v.y * r));
-                hv[h_slot(4 * i + 2)] = __float2half_rn(bf16_round(v.z * r));
-                hv[h_slot(4 * i + 3)] = __float2half_rn(bf16_round(v.w * r));
-            }
+            for (int w = 0; w < 8; ++w) tsum += red[w][b];
+            rn[b] = rsqrt_ieee(tsum / (float)K + kEps);
         }
     } else {
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            __half* hv = hs + (size_t)b * hld;
-            const uint32_t* iv = reinterpret_cast<const uint32_t*>(p.in + (size_t)b * p.ld_in);
-            for (int i = threadIdx.x; i < K / 2; i += kGemvThreads) {
-                const uint32_t w2 = b < users ? iv[i] : 0u;
-                hv[h_slot(2 * i)] = __float2half_rn(bf16lo(w2));
-                hv[h_slot(2 * i + 1)] = __float2half_rn(bf16hi(w2));
+        for (int b = 0; b < B; ++b) rn[b] = 1.f;
+        __syncthreads();  // the zeroed operand before the writes below
+    }
+    // one warp per (user, K block): lane holds K positions 4 * lane .. + 3 of the block
+    for (int pr = warp; pr < B * nwin; pr += 8) {
+        const int b = pr % B, ws = pr / B;
+        int kb = kb_start + ws;
+        if (kb >= nkb) kb -= nkb;
+        float h[4] = {0.f, 0.f, 0.f, 0.f};
+        if (b < users) {
+            if (PRO == PRO_BF16) {
+                const uint2 v = *reinterpret_cast<const uint2*>(p.in + (size_t)b * p.ld_in + kb * 128 + 4 * lane);
+                h[0] = bf16lo(v.x);
+                h[1] = bf16hi(v.x);
+                h[2] = bf16lo(v.y);
+                h[3] = bf16hi(v.y);
+            } else {
+                const float4* xp = reinterpret_cast<const float4*>(p.x + (size_t)b * K + kb * 128) + lane;
+                float4 v = *xp;
+                if (PRO == PRO_RMSNORM_ADD) {
+                    const float4 r = reinterpret_cast<const float4*>(p.red + (size_t)b * K + kb * 128)[lane];
+                    v.x += r.x;
+                    v.y += r.y;
+                    v.z += r.z;
+                    v.w += r.w;
+                }
+                // h = bf16(x * r)
+                float rb = 1.f;
+#pragma unroll
+                for (int bb = 0; bb < B; ++bb)
+                    if (bb == b) rb = rn[bb];
+                h[0] = bf16_round(v.x * rb);
+                h[1] = bf16_round(v.y * rb);
+                h[2] = bf16_round(v.z * rb);
+                h[3] = bf16_round(v.w * rb);
             }
         }
+        const float m = warp_max(fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3]))));
+        int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
+        e = max(e, -100);
+        const float f = __uint_as_float((uint32_t)(127 + 7 - e) << 23);    // 2^(7-E): max|h| * f in [128, 256)
+        const float fi = __uint_as_float((uint32_t)(127 - 7 + e) << 23);   // 2^(E-7)
+        float y[4], lo[4];
+        uint32_t hi_w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+            y[j] = h[j] * f;
+            y[j + 1] = h[j + 1] * f;
+            const uint32_t hb = e4m3x2(y[j], y[j + 1]);
+            const float2 hv = e4m3x2_f32(hb);
+            lo[j] = y[j] - hv.x;  // exact
+            lo[j + 1] = y[j + 1] - hv.y;
+            hi_w |= hb << (8 * j);
+        }
+        const uint32_t lo_w = e4m3x2(lo[0], lo[1]) | (e4m3x2(lo[2], lo[3]) << 16);
+        uint8_t* dst = act + (size_t)(b >> 2) * nkw * kActKb + (size_t)ws * kActKb + (lane >> 2) * 128 +
+                       (2 * (b & 3)) * 16 + (lane & 3) * 4;
+        *reinterpret_cast<uint32_t*>(dst) = hi_w;
+        *reinterpret_cast<uint32_t*>(dst + 16) = lo_w;
+        if (lane == 0) ainv[ws * 8 + b] = (b < users && m > 0.f) ? fi : 0.f;
     }
+    fence_proxy_async();  // the operand written by generic stores, read by the tensor core (async proxy)
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
 
-    // ---- main loop: one 16 x 128 unit at a time
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int cur = -1;  // tile being accumulated
-    bool ok = true;
-    const bool rows_b = (g & 3) >= 2;  // rows g and g + 8 are both of a quad's second pair (the up rows of gate|up)
-    const bool hrow = g < B;
-    const __half* hg = hs + (size_t)(hrow ? g : 0) * hld;
-
-    auto split_tile = [&](int T) {
-        const int ufirst = T * nkbl, ulast = ufirst + nkbl - 1;
-        return warp_of_unit(ufirst, base, rem) != warp_of_unit(ulast, base, rem);
-    };
-    auto flush = [&](int T, const float* a4) {
-        // the tile's units may be spread over several warps: parts land in the workspace, the last writer sums
-        const int ufirst = T * nkbl, ulast = ufirst + nkbl - 1;
-        const int w0 = warp_of_unit(ufirst, base, rem), w1 = warp_of_unit(ulast, base, rem);
-        float v[4] = {a4[0], a4[1], a4[2], a4[3]};
-        bool mine = true;
-        if (w0 != w1) {
-            const int slot = (T == u0 / nkbl) ? 0 : 1;
-            float* dst = p.part + ((size_t)gw * 2 + slot) * 128;
-            reinterpret_cast<float4*>(dst)[lane] = make_float4(a4[0], a4[1], a4[2], a4[3]);
-            __threadfence();
-            __syncwarp();
-            int tk = 0;
-            if (lane == 0) tk = atomicAdd(p.ticket + T, 1);
-            tk = __shfl_sync(0xffffffffu, tk, 0);
-            mine = (tk == w1 - w0);
-            if (mine) {
+    int issued = min(NS, cnt);
+    if (warp == 0) {
+        // ---- producer
+        if (lane == 0) {
+            for (int i = NS; i < cnt; ++i) {
+                if (!mbar_wait(&empty[i % NS], ((i / NS) - 1) & 1, p.err)) break;
+                issue(i);
+                issued = i + 1;
+            }
+            if (p.next_w != nullptr && p.next_prefetch > 0) {
+                const int nb = p.next_units / G, nr = p.next_units % G;
+                const int nu0 = blockIdx.x * nb + min((int)blockIdx.x, nr), ncnt = nb + ((int)blockIdx.x < nr ? 1 : 0);
+                const int pf = min(ncnt, p.next_prefetch);
+                if (pf > 0) l2_prefetch_share(p.next_w + (size_t)nu0 * kUnitBytes, (size_t)pf * kUnitBytes, 0, 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            const uint32_t ring_a = smem_addr(ring), act_a = smem_addr(act);
+            const uint32_t sbo_b = B > 4 ? (uint32_t)(nkw * kActKb) : 0u;  // users 4..7 (columns 8..15)
+            int ws = 0;
+            for (int i = 0; i < cnt; ++i) {
+                const int slot = i % NS, d = i % kDSlots;
+                if (!mbar_wait(&full[slot], (i / NS) & 1, p.err)) break;
+                if (i >= kDSlots && !mbar_wait(&dempty[d], ((i / kDSlots) - 1) & 1, p.err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const uint64_t ad = smem_desc(ring_a + slot * kUnitBytes + m * 256, 128, 1024);
+                    const uint64_t bd = smem_desc(act_a + ws * kActKb + m * 256, 128, sbo_b);
+                    tc_mma_f8(tmem + d * 16, ad, bd, m > 0 ? 1u : 0u);
+                }
+                tc_commit(&empty[slot]);
+                tc_commit(&dfull[d]);
+                if (++ws == nkb) ws = 0;
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.err);
+        }
+    } else if (warp >= 4) {
+        // ---- epilogue: TMEM lanes 32q .. 32q + 31 (the warp's TMEM quarter), one tile row per thread
+        const int q = warp & 3, row = 32 * q + lane;
+        const size_t tstride = kSelBytes + (size_t)nkb * 32;
+        bool ok = true;
+        float acc[B], first_acc[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] = first_acc[b] = 0.f;
+        int cur = -1, first_tile = -1;
+        const int first_T = u0 / nkb;
+        auto split_tile = [&](int T) { return cta_of_unit(T * nkb, base, rem) != cta_of_unit(T * nkb + nkb - 1, base, rem); };
+        auto flush = [&](int T, float* v) {
+            const int c0 = cta_of_unit(T * nkb, base, rem), c1 = cta_of_unit(T * nkb + nkb - 1, base, rem);
+            if (c0 != c1) {
+                const int slot = (T == first_T) ? 0 : 1;
+                float* dst = p.part + ((size_t)blockIdx.x * 2 + slot) * 8 * 128;
+#pragma unroll
+                for (int b = 0; b < B; ++b) dst[b * 128 + row] = v[b];
                 __threadfence();
-                v[0] = v[1] = v[2] = v[3] = 0.f;
-                for (int ww = w0; ww <= w1; ++ww) {
-                    const int wu0 = ww * base + min(ww, rem);
-                    const int sl = (T == wu0 / nkbl) ? 0 : 1;
-                    const float4 q = __ldcg(reinterpret_cast<const float4*>(p.part + ((size_t)ww * 2 + sl) * 128) + lane);
-                    v[0] += q.x;
-                    v[1] += q.y;
-                    v[2] += q.z;
-                    v[3] += q.w;
+                bar_sync(1, 128);
+                if (row == 0) *tk_slot = atomicAdd(p.ticket + T, 1);
+                bar_sync(1, 128);
+                if (*tk_slot != c1 - c0) return;
+                __threadfence();
+#pragma unroll
+                for (int b = 0; b < B; ++b) v[b] = 0.f;
+                for (int c = c0; c <= c1; ++c) {
+                    const int cu0 = c * base + min(c, rem);
+                    const int sl = (T == cu0 / nkb) ? 0 : 1;
+                    const float* src = p.part + ((size_t)c * 2 + sl) * 8 * 128;
+#pragma unroll
+                    for (int b = 0; b < B; ++b) v[b] += __ldcg(src + b * 128 + row);
                 }
-                if (lane == 0) p.ticket[T] = 0;
+                if (row == 0) p.ticket[T] = 0;
             }
-        }
-        if (!mine) return;
-        // epilogue from the fragment: v[0], v[1] = (row g, users 2t, 2t+1); v[2], v[3] = (row g + 8, same)
-        const int r0 = T * 16 + g, r1 = r0 + 8;
-        if (EPI == EPI_SILU_MUL) {
-            // quads of rows are gate(j), gate(j+1), up(j), up(j+1): the up partner of row g is row g + 2 (lane + 8)
-            float up[4];
+            const int r = T * kTileRows + row;
+            if (EPI == EPI_SILU_MUL) {
+                // quads of rows are gate(j), gate(j+1), up(j), up(j+1): the up partner of row r is r + 2
+                float up[B];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) up[i] = __shfl_down_sync(0xffffffffu, v[i], 8);
-            if ((g & 3) < 2) {
+                for (int b = 0; b < B; ++b) up[b] = __shfl_down_sync(0xffffffffu, v[b], 2);
+                if ((row & 3) < 2) {
+                    const int col = 2 * (r >> 2) + (r & 3);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int user = 2 * t + (i & 1);
-                    const int quad = T * 4 + (g >> 2) + (i >= 2 ? 2 : 0);
-                    const int col = 2 * quad + (g & 3);
-                    if (user < users && 2 * col < p.rows)
-                        reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)user * p.ld_out + col] =
-                            __float2bfloat16_rn(silu_f(v[i]) * up[i]);
+                    for (int b = 0; b < B; ++b)
+                        if (b < users && 2 * col < p.rows)
+                            reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)b * p.ld_out + col] =
+                                __float2bfloat16_rn(silu_f(v[b]) * up[b]);
                 }
-            }
-        } else {
+            } else if (r < p.rows) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int user = 2 * t + (i & 1);
-                const int row = i >= 2 ? r1 : r0;
-                if (user < users && row < p.rows) {
+                for (int b = 0; b < B; ++b) {
+                    if (b >= users) break;
                     if (EPI == EPI_BF16) {
-                        reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)user * p.ld_out + row] = __float2bfloat16_rn(v[i]);
+                        reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)b * p.ld_out + r] = __float2bfloat16_rn(v[b]);
                     } else if (EPI == EPI_RESID) {
-                        float* o = reinterpret_cast<float*>(p.out) + (size_t)user * p.ld_out + row;
-                        *o = v[i] + *o;
+                        float* o = reinterpret_cast<float*>(p.out) + (size_t)b * p.ld_out + r;
+                        *o = v[b] + *o;
                     } else {
-                        reinterpret_cast<float*>(p.out)[(size_t)user * p.ld_out + row] = v[i];
+                        reinterpret_cast<float*>(p.out)[(size_t)b * p.ld_out + r] = v[b];
                     }
                 }
             }
-        }
-    };
+        };
 
-    // a split first tile is held back and flushed after the stream (its atomics never stall the ring)
-    float first_acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int first_tile = -1;
-    int tT = u0 / nkbl, tK = u0 % nkbl;  // (tile, block) of the next unit: a warp's units are consecutive
-    // the unit scales of a stage are loaded one stage ahead (they never stall the stage's math)
-    auto unit_scales = [&](int s2, float* out2) {
-        const int a2 = u0 + s2 * kStageUnits;
-#pragma unroll
-        for (int i = 0; i < kStageUnits; ++i) {
-            out2[i] = 0.f;
-            if (s2 < nst && a2 + i < u0 + cnt) {
-                const int uu = a2 + i, T2 = uu / nkbl, kb2 = p.kb0 + uu % nkbl;
-                const float2 v = __ldg(p.uscale + (size_t)T2 * p.nkb + kb2);
-                out2[i] = rows_b ? v.y : v.x;
+        // the scale of the next unit is loaded one unit ahead
+        int T = u0 / nkb, kb = kb_start, ws = 0;
+        int sel = p.table[(size_t)T * tstride + row];
+        float s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)T * tstride + kSelBytes) + kb * 8 + sel);
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+        for (int i = 0; i < cnt; ++i) {
+            const float s = s_next;
+            const int Tc = T, wsc = ws;
+            if (++kb == nkb) {
+                kb = 0;
+                ++T;
+                if (i + 1 < cnt) sel = p.table[(size_t)T * tstride + row];
             }
-        }
-    };
-    float sc_cur[kStageUnits], sc_next[kStageUnits];
-    unit_scales(0, sc_cur);
-    for (int s = 0; s < nst; ++s) {
-        unit_scales(s + 1, sc_next);
-        const int slot = s % NS;
-        if (ok) ok = mbar_wait(&bars[slot], (s / NS) & 1, p.err);
-        const int a = u0 + s * kStageUnits, n = min(kStageUnits, u0 + cnt - a);
-        // the stage's weights go to registers and its slot is refilled at once: every stage of the ring stays in
-        // flight while this one is computed (the memory latency is covered by the whole ring, not all but one)
-        uint4 wr[kStageUnits][2][2];
-        if (ok) {
-            const uint8_t* st = wring + (size_t)slot * kStageBytes;
+            if (++ws == nkb) ws = 0;
+            if (i + 1 < cnt)
+                s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)T * tstride + kSelBytes) + kb * 8 + sel);
+            // after a timeout the warp keeps its place in the loop without waiting (its results are void, the
+            // error word is set): every epilogue warp reaches the same tile flushes and their named barriers
+            const int d = i % kDSlots;
+            if (ok && !mbar_wait(&dfull[d], (i / kDSlots) & 1, p.err)) ok = false;
+            tc_fence_after();
+            constexpr int NC = B <= 4 ? 2 * B : 16;
+            float v[NC];
+            tmem_load<NC>(taddr + d * 16, v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dempty[d]);
+            if (Tc != cur) {
+                if (cur >= 0) {
+                    if (first_tile < 0 && cur == first_T && split_tile(cur)) {
+                        first_tile = cur;
 #pragma unroll
-            for (int i = 0; i < kStageUnits; ++i) {
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const int sw = (half ^ (g & 1)) * 64 + 16 * t;  // rows g and g + 8 share the parity
-                    if (i < n) {
-                        wr[i][half][0] = lds128(st + i * kUnitBytes + g * 128 + sw);
-                        wr[i][half][1] = lds128(st + i * kUnitBytes + (g + 8) * 128 + sw);
+                        for (int b = 0; b < B; ++b) first_acc[b] = acc[b];
+                    } else {
+                        flush(cur, acc);
                     }
                 }
+#pragma unroll
+                for (int b = 0; b < B; ++b) acc[b] = 0.f;
+                cur = Tc;
             }
+#pragma unroll
+            for (int b = 0; b < B; ++b) acc[b] = fmaf(v[2 * b] + v[2 * b + 1], s * ainv[wsc * 8 + b], acc[b]);
         }
-        __syncwarp();
-        if (lane == 0 && ok && s + NS < nst) {
-            fence_proxy_async();
-            issue(s + NS);
-        }
-        if (ok) {
-#pragma unroll
-            for (int i = 0; i < kStageUnits; ++i) {
-                if (i >= n) break;
-                const int T = tT, kb = p.kb0 + tK;
-                if (++tK == nkbl) {
-                    tK = 0;
-                    ++tT;
-                }
-                if (T != cur) {
-                    if (cur >= 0) {
-                        if (first_tile < 0 && cur == u0 / nkbl && split_tile(cur)) {
-                            first_tile = cur;
-                            first_acc[0] = acc[0];
-                            first_acc[1] = acc[1];
-                            first_acc[2] = acc[2];
-                            first_acc[3] = acc[3];
-                        } else {
-                            flush(cur, acc);
-                        }
-                    }
-                    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-                    cur = T;
-                }
-                const float sc = sc_cur[i];
-                // 4 independent accumulators (one per word m): short dependency chains
-                float d[4][4];
-#pragma unroll
-                for (int m = 0; m < 4; ++m) d[m][0] = d[m][1] = d[m][2] = d[m][3] = 0.f;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const uint4 wa = wr[i][half][0], wb = wr[i][half][1];
-                    uint4 h0 = make_uint4(0, 0, 0, 0), h1 = make_uint4(0, 0, 0, 0);
-                    if (hrow) {
-                        const __half* hp = hg + (kb - p.kb0) * 128 + half * 64 + 16 * t;
-                        h0 = lds128(hp);
-                        h1 = lds128(hp + 8);
-                    }
-                    uint32_t a0, a1, a2, a3;
-                    // words 0, 1: the conversion unit; words 2, 3: integer ops (values x 2^-8)
-                    cvt_word_xu(wa.x, a0, a2);
-                    cvt_word_xu(wb.x, a1, a3);
-                    mma_f16(d[0], a0, a1, a2, a3, h0.x, h0.y);
-                    cvt_word_xu(wa.y, a0, a2);
-                    cvt_word_xu(wb.y, a1, a3);
-                    mma_f16(d[1], a0, a1, a2, a3, h0.z, h0.w);
-                    cvt_word_alu(wa.z, a0, a2);
-                    cvt_word_alu(wb.z, a1, a3);
-                    mma_f16(d[2], a0, a1, a2, a3, h1.x, h1.y);
-                    cvt_word_alu(wa.w, a0, a2);
-                    cvt_word_alu(wb.w, a1, a3);
-                    mma_f16(d[3], a0, a1, a2, a3, h1.z, h1.w);
-                }
-#pragma unroll
-                for (int i2 = 0; i2 < 4; ++i2) {
-                    const float v = (d[0][i2] + d[1][i2]) + 256.f * (d[2][i2] + d[3][i2]);
-                    acc[i2] = fmaf(v, sc, acc[i2]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kStageUnits; ++i) sc_cur[i] = sc_next[i];
-    }
-    if (!ok && lane == 0) {
-        // never leave a copy in flight into shared memory that is about to be released
-        for (int s = max(0, nst - NS); s < nst; ++s) mbar_wait(&bars[s % NS], (s / NS) & 1, nullptr);
-    }
-    // the stream is done: pull the start of this warp's range of the next projection into L2
-    if (lane == 0 && p.next_w != nullptr && p.next_prefetch > 0) {
-        const int nb = p.next_units / W, nr = p.next_units % W;
-        const int nu0 = gw * nb + min(gw, nr), ncnt = nb + (gw < nr ? 1 : 0);
-        const int pre = min(ncnt, p.next_prefetch);
-        if (pre > 0) l2_prefetch_share(p.next_w + (size_t)nu0 * kUnitBytes, (size_t)pre * kUnitBytes, 0, 1);
-    }
-    if (ok) {
         if (cur >= 0) flush(cur, acc);
         if (first_tile >= 0) flush(first_tile, first_acc);
+    }
+    if (warp == 0 && lane == 0) {
+        // never release shared memory with a copy still landing in it
+        for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, nullptr);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -471,48 +556,55 @@ static cudaError_t launch_pe(const GemvParams& p, int Bt, int grid, size_t smem,
     }
 }
 
-// smem budget of one GEMV CTA: two CTAs (the finishing kernel's and the next one's) share an SM under PDL
-constexpr size_t kGemvSmemBudget = 112 * 1024;
-constexpr size_t kGemvSmemMax = 220 * 1024;
+// shared memory of one GEMV CTA: half an SM's (a second CTA -- the next projection's, under programmatic
+// dependent launch -- fits beside it and starts its weight stream during this one's tail); past that, up to
+// the per-CTA maximum with a shallower ring
+constexpr size_t kGemvSmemBudget = 113 * 1024;
+constexpr size_t kGemvSmemMax = 227 * 1024;
+constexpr int kMinStages = 3;
 
 static int bt_of(int users) { return users == 1 ? 1 : users == 2 ? 2 : users <= 4 ? 4 : 8; }
 
-// K blocks one launch may cover at this row count (the f16 activations of the covered K sit in shared memory)
-int gemv_max_kb(int users) {
-    const int Bt = bt_of(users);
-    for (int kb = 160; kb >= 1; --kb)
-        if (gemv_smem_bytes(Bt, kb * 128, 2) <= kGemvSmemMax) return kb;
-    return 1;
-}
+// workspace: the tile tickets at a fixed place (they must read zero at every launch, whatever the grid or the
+// weight: each launch leaves the ones it used at zero), then a [grid][2][8][128] fp32 part buffer per launch
+constexpr int kGemvMaxTiles = 4096;  // 524,288 rows
+size_t gemv_workspace_bytes(int grid) { return (size_t)kGemvMaxTiles * 4 + (size_t)grid * 2 * 8 * 128 * 4; }
 
-size_t gemv_workspace_bytes(int grid, int max_tiles) {
-    return (size_t)grid * kGemvWarps * 2 * 128 * 4 + 256 + (size_t)max_tiles * 4;
+// grid actually launched for a request of `grid` CTAs: at most one per unit, and enough that every CTA's
+// activation window fits in shared memory
+int gemv_grid(int users, int rows_pad, int K, int grid) {
+    const int U = (rows_pad / kTileRows) * (K / 128);
+    const int Bt = bt_of(users);
+    int g = grid < 1 ? 1 : grid;
+    if (g > U) g = U;
+    for (;;) {
+        const int nkw = std::min((U + g - 1) / g, K / 128);
+        if (gemv_smem_bytes(Bt, nkw, kMinStages) <= kGemvSmemMax || g >= U) return g;
+        g = std::min(U, g + g / 4 + 1);
+    }
 }
 
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, int kb0, int kb1, const qres_weight* next, int next_prefetch) {
-    if (users < 1 || users > kMaxRows || w.K % 128 != 0 || w.rows_pad % 16 != 0) return cudaErrorInvalidValue;
+                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch) {
+    if (users < 1 || users > kMaxRows || w.K % 128 != 0 || w.rows_pad % kTileRows != 0 || w.rows_pad < w.rows ||
+        w.rows_pad > kGemvMaxTiles * kTileRows)
+        return cudaErrorInvalidValue;
     const int Bt = bt_of(users);
     const int nkb = w.K / 128;
-    if (kb1 <= 0) kb1 = nkb;
-    if (kb0 < 0 || kb0 >= kb1 || kb1 > nkb) return cudaErrorInvalidValue;
-    if (kb0 != 0 && pro != PRO_BF16) return cudaErrorInvalidValue;  // rmsnorm needs the whole row
-    const int tiles = w.rows_pad / 16;
-    if (grid < 1) grid = 1;
-    if (work == nullptr || work_bytes < gemv_workspace_bytes(grid, tiles)) return cudaErrorInvalidValue;
+    const int tiles = w.rows_pad / kTileRows;
+    grid = gemv_grid(users, w.rows_pad, w.K, grid);
+    if (work == nullptr || work_bytes < gemv_workspace_bytes(grid)) return cudaErrorInvalidValue;
     GemvParams p;
     p.w = static_cast<const uint8_t*>(w.data);
-    p.uscale = reinterpret_cast<const float2*>(w.uscale);
+    p.table = reinterpret_cast<const uint8_t*>(w.uscale);
     p.rows = w.rows;
     p.tiles = tiles;
-    p.K = (kb1 - kb0) * 128;  // the activations this launch reads
+    p.K = w.K;
     p.nkb = nkb;
-    p.kb0 = kb0;
-    p.kb1 = kb1;
     p.users = users;
     p.x = pro != PRO_BF16 ? static_cast<const float*>(in) : nullptr;
-    p.in = pro == PRO_BF16 ? static_cast<const uint16_t*>(in) + (size_t)kb0 * 128 : nullptr;
+    p.in = pro == PRO_BF16 ? static_cast<const uint16_t*>(in) : nullptr;
     p.ld_in = ld_in;
     p.red = red;
     p.x_out = x_out;
@@ -521,19 +613,21 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.ld_out = ld_out;
     p.err = err;
     p.next_w = next ? static_cast<const uint8_t*>(next->data) : nullptr;
-    p.next_units = next ? (next->rows_pad / 16) * (next->K / 128) : 0;
+    p.next_units = next ? (next->rows_pad / kTileRows) * (next->K / 128) : 0;
     p.next_prefetch = next ? next_prefetch : 0;
     uint8_t* wk = static_cast<uint8_t*>(work);
-    p.part = reinterpret_cast<float*>(wk);
-    p.ticket = reinterpret_cast<int*>(wk + (size_t)grid * kGemvWarps * 2 * 128 * 4 + 256);
-    // ring depth: as deep as the budget allows (two CTAs per SM), at least 2 stages per warp
-    const size_t hb = gemv_h_bytes(Bt, p.K);
-    int ns = hb + 512 < kGemvSmemBudget ? (int)((kGemvSmemBudget - 512 - hb) / ((size_t)kGemvWarps * kStageBytes)) : 0;
-    if (ns < 2) ns = hb + 512 < kGemvSmemMax ? (int)((kGemvSmemMax - 512 - hb) / ((size_t)kGemvWarps * kStageBytes)) : 0;
-    if (ns < 2) return cudaErrorInvalidValue;
+    p.ticket = reinterpret_cast<int*>(wk);
+    p.part = reinterpret_cast<float*>(wk + (size_t)kGemvMaxTiles * 4);
+    const int U = tiles * nkb;
+    p.nkw = std::min((U + grid - 1) / grid, nkb);
+    // ring depth: as deep as half an SM allows, else as deep as the per-CTA maximum allows
+    const size_t fixed = gemv_smem_bytes(Bt, p.nkw, 0);
+    int ns = fixed < kGemvSmemBudget ? (int)((kGemvSmemBudget - fixed) / kUnitBytes) : 0;
+    if (ns < kMinStages) ns = fixed < kGemvSmemMax ? (int)((kGemvSmemMax - fixed) / kUnitBytes) : 0;
+    if (ns < kMinStages) return cudaErrorInvalidValue;
     ns = ns > kMaxStages ? kMaxStages : ns;
     p.nstages = ns;
-    const size_t smem = gemv_smem_bytes(Bt, p.K, ns);
+    const size_t smem = gemv_smem_bytes(Bt, p.nkw, ns);
     if (pro == PRO_RMSNORM && epi == EPI_BF16) return launch_pe<PRO_RMSNORM, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_SILU_MUL) return launch_pe<PRO_RMSNORM, EPI_SILU_MUL>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_BF16) return launch_pe<PRO_RMSNORM_ADD, EPI_BF16>(p, Bt, grid, smem, st, pdl);

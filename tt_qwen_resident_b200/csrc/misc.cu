@@ -12,21 +12,22 @@
 namespace qres {
 
 // ------------------------------------------------------------------------------------------------ tiling
-// dst[(T * nkb + kb) * 2048 + r * 128 + ((half ^ (r & 1)) * 64) + i] = src[(16 T + r) * K + kb * 128 + half * 64 + i]
+// 128-row tiles, 128-K units of 16 KB back to back per tile, inside a unit the tensor core's no-swizzle K-major
+// core matrices: dst[(T * nkb + kb) * 16384 + (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16] =
+// src[(128 T + r) * K + 128 kb + c], zero past the last row. One thread per 16-byte granule (one core-matrix row).
 __global__ void tile_weight_kernel(const uint8_t* __restrict__ src, int rows, int K, uint8_t* __restrict__ dst,
                                    size_t total16) {
     const int nkb = K / 128;
     for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < total16; v += (size_t)gridDim.x * blockDim.x) {
         const size_t off = v * 16;
-        const size_t unit = off / 2048;
-        const int inner = (int)(off % 2048);
+        const size_t unit = off / 16384;
+        const int inner = (int)(off % 16384);
         const size_t T = unit / nkb;
         const int kb = (int)(unit % nkb);
-        const int r = inner / 128, pos = inner % 128;
-        const int half = (pos / 64) ^ (r & 1), i = pos % 64;
-        const size_t row = T * 16 + r;
+        const int r = (inner / 1024) * 8 + (inner % 128) / 16, c = ((inner % 1024) / 128) * 16;
+        const size_t row = T * 128 + r;
         uint4 val = make_uint4(0, 0, 0, 0);
-        if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)kb * 128 + half * 64 + i);
+        if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)kb * 128 + c);
         *reinterpret_cast<uint4*>(dst + off) = val;
     }
 }
@@ -298,7 +299,7 @@ static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, 
 }
 
 cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st) {
-    const int rows_pad = (rows + 15) & ~15;
+    const int rows_pad = (rows + 127) & ~127;
     const size_t total16 = (size_t)rows_pad * K / 16;
     tile_weight_kernel<<<1024, 256, 0, st>>>(src, rows, K, dst, total16);
     return cudaGetLastError();

@@ -25,9 +25,8 @@
 namespace qres {
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, int kb0, int kb1, const qres_weight* next, int next_prefetch);
-size_t gemv_workspace_bytes(int grid, int max_tiles);
-int gemv_max_kb(int users);
+                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch);
+size_t gemv_workspace_bytes(int grid);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -181,14 +180,6 @@ struct Carve {
     size_t err, xb, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
 };
 
-int max_tiles(const qres_ctx* c) {
-    int rows = kHidden;
-    rows = std::max(rows, 2 * c->ic);
-    rows = std::max(rows, c->ld_y);
-    rows = std::max(rows, c->vocab_local);
-    return (rows + 15) / 16;
-}
-
 Carve carve(const qres_ctx* c) {
     Carve k;
     const int R = c->cfg.rows;
@@ -208,7 +199,7 @@ Carve carve(const qres_ctx* c) {
     k.gathered = take((size_t)c->nranks * R * 2 * QRES_TOPK * 4);
     k.attn = take(attn_workspace_bytes(c->nranks, R, c->attn_chunks));
     k.topk = take(c->vocab_local ? topk_workspace_bytes(R, c->topk_blk) : 0);
-    k.gemv_bytes = gemv_workspace_bytes(2 * c->sm_count, max_tiles(c));
+    k.gemv_bytes = gemv_workspace_bytes(2 * c->sm_count);
     k.gemv = take(k.gemv_bytes);
     k.total = off;
     return k;
@@ -216,7 +207,7 @@ Carve carve(const qres_ctx* c) {
 
 qres_status check_weight(qres_ctx* c, const qres_weight* w, int rows, int K, const char* what) {
     if (!w || !w->data || !w->uscale) return fail(c, QRES_ERR_ARG, "%s: null pointer", what);
-    if (w->rows != rows || w->K != K || w->rows_pad != ((rows + 15) & ~15))
+    if (w->rows != rows || w->K != K || w->rows_pad != ((rows + 127) & ~127))
         return fail(c, QRES_ERR_ARG, "%s: shape rows=%d K=%d rows_pad=%d (want rows=%d K=%d)", what, w->rows, w->K,
                     w->rows_pad, rows, K);
     return QRES_OK;
@@ -464,35 +455,27 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             if (order[i] == w) return order[(i + 1) % order.size()];
         return nullptr;
     };
-    const int kPrefetchUnits = 16;  // 32 KB per warp
+    const int kPrefetchUnits = 2;  // 32 KB per CTA
     auto gemv = [&](const qres_weight& w, int pro, const void* in, int ld_in, int epi, void* out, int ld_out,
-                    const float* red, float* x_out, int kb0, int kb1, const char* what) -> qres_status {
+                    const float* red, float* x_out, const char* what) -> qres_status {
         return K(gemv_launch(w, R, pro, in, ld_in, epi, out, ld_out, grid, c->err, st, true, red, x_out, c->gemv_work,
-                             c->gemv_work_bytes, kb0, kb1, next_of(&w), kPrefetchUnits),
+                             c->gemv_work_bytes, next_of(&w), kPrefetchUnits),
                  what);
     };
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
         if (pending) {
-            qres_status s = gemv(w, 2, cur, kHidden, epi, out, ld_out, c->partial, other, 0, 0, what);
+            qres_status s = gemv(w, 2, cur, kHidden, epi, out, ld_out, c->partial, other, what);
             std::swap(cur, other);
             pending = false;
             return s;
         }
-        return gemv(w, 0, cur, kHidden, epi, out, ld_out, nullptr, nullptr, 0, 0, what);
+        return gemv(w, 0, cur, kHidden, epi, out, ld_out, nullptr, nullptr, what);
     };
-    // a row-parallel projection: residual update (one rank) or fp32 partial + all-reduce (TP). When the rows'
-    // activations exceed shared memory (8 users x K 17408) the K range is covered by several launches, each
-    // adding its part in order.
+    // a row-parallel projection: residual update (one rank) or fp32 partial + all-reduce (TP)
     auto row_parallel = [&](const qres_weight& w, const uint16_t* in, const char* what) -> qres_status {
-        const int nkb = w.K / 128, step = gemv_max_kb(R);
-        for (int kb0 = 0; kb0 < nkb; kb0 += step) {
-            const int kb1 = std::min(nkb, kb0 + step);
-            const int epi = !tp ? 2 : (kb0 == 0 ? 3 : 2);
-            qres_status s = gemv(w, 1, in, w.K, epi, tp ? c->partial : cur, kHidden, nullptr, nullptr, kb0, kb1, what);
-            if (s) return s;
-        }
-        if (!tp) return QRES_OK;
-        qres_status s = allreduce();
+        qres_status s = gemv(w, 1, in, w.K, tp ? 3 : 2, tp ? c->partial : cur, kHidden, nullptr, nullptr, what);
+        if (s || !tp) return s;
+        s = allreduce();
         pending = true;
         return s;
     };
@@ -607,14 +590,15 @@ int32_t qres_step_launches(const qres_ctx* c) { return c ? c->launches : 0; }
 // ---- single kernels ----
 
 qres_status qres_gemv_workspace_size(int32_t grid, int32_t rows_pad, size_t* bytes) {
-    if (!bytes || rows_pad < 16) return fail(nullptr, QRES_ERR_ARG, "qres_gemv_workspace_size: bad argument");
+    if (!bytes || rows_pad < 128 || rows_pad % 128 || rows_pad > 4096 * 128)
+        return fail(nullptr, QRES_ERR_ARG, "qres_gemv_workspace_size: bad argument");
     if (grid <= 0) {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&grid, cudaDevAttrMultiProcessorCount, dev);
         grid *= 2;
     }
-    *bytes = gemv_workspace_bytes(grid, (rows_pad + 15) / 16);
+    *bytes = gemv_workspace_bytes(grid);
     return QRES_OK;
 }
 
@@ -629,21 +613,9 @@ qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const voi
         grid *= 2;  // two CTAs per SM
     }
     const int ld_out = epi == 1 ? w->rows / 2 : w->rows;
-    const int nkb = w->K / 128, step = pro == 1 ? gemv_max_kb(rows) : nkb;
-    if (pro == 0 && nkb > gemv_max_kb(rows)) return fail(nullptr, QRES_ERR_ARG, "qres_gemv: rows x K too large for rmsnorm");
-    for (int kb0 = 0; kb0 < nkb; kb0 += step) {
-        const int kb1 = std::min(nkb, kb0 + step);
-        // a K range after the first accumulates into the output (fp32 epilogues only)
-        int e = epi;
-        if (kb0 > 0) {
-            if (epi != 2 && epi != 3) return fail(nullptr, QRES_ERR_ARG, "qres_gemv: K split needs an fp32 epilogue");
-            e = 2;
-        }
-        cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, e, out, ld_out, grid, err,
-                                     static_cast<cudaStream_t>(stream), false, nullptr, nullptr, work, work_bytes, kb0, kb1,
-                                     nullptr, 0);
-        if (ce != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(ce));
-    }
+    cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, epi, out, ld_out, grid, err, static_cast<cudaStream_t>(stream),
+                                 false, nullptr, nullptr, work, work_bytes, nullptr, 0);
+    if (ce != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(ce));
     return QRES_OK;
 }
 

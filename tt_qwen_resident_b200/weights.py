@@ -11,8 +11,8 @@ Canonical layout (projection weights [out_features, in_features], FP8-e4m3 + one
   attn in-proj [14336, 5120]  rows q(24x256) | gate(24x256) | k(4x256) | v(4x256)
   out-proj [5120, 6144], gate / up [17408, 5120], down [5120, 17408], lm_head [vocab, 5120]
 A rank's projection keeps the canonical quantisation: its rows (and K range) are gathered, every row keeps
-the scale of its 128-row block (streamed per 16 x 128 unit, ``uscale``), and the bytes are re-laid into the
-GEMV's tile/unit layout.
+the scale of its canonical 128-row block, and the bytes are re-laid into the GEMV's layout (128-row tiles of
+16 KB units, see ``scale_table`` for the scales).
 """
 import ctypes
 import math
@@ -48,13 +48,13 @@ class GemvWeight:
     """one rank's projection in the GEMV layout (device tensors)"""
 
     data: torch.Tensor  # uint8 [rows_pad * K]
-    uscale: torch.Tensor  # fp32 [rows_pad / 16, K / 128, 2]: per 16-row x 128-K unit, the scale of rows r % 4 < 2, >= 2
+    uscale: torch.Tensor  # uint8 [rows_pad / 128, 128 + (K / 128) * 32]: the scale table (scale_table)
     rows: int
     K: int
 
     @property
     def rows_pad(self):
-        return (self.rows + 15) // 16 * 16
+        return (self.rows + 127) // 128 * 128
 
     def cstruct(self):
         return _lib.Weight(self.data.data_ptr(), self.uscale.data_ptr(), self.rows, self.rows_pad, self.K, 0)
@@ -131,10 +131,38 @@ def quantize(w):
     return FP8Matrix(q, s)
 
 
+def scale_table(blk, scales, kb0, kb1):
+    """The GEMV's scale table of one projection: blk = canonical 128-row block of every local row (LongTensor,
+    length rows), scales = the canonical fp32 block scales [row blocks][K / 128], K blocks [kb0, kb1) kept.
+    Per 128-row tile: 128 bytes of row selectors (row r's block is the tile's slot sel[r] of at most 8), then for
+    every K block the 8 slots' scales (fp32; unused slots 0). uint8 [tiles, 128 + (kb1 - kb0) * 32]."""
+    n = blk.numel()
+    tiles = -(-n // 128)
+    b = torch.empty(tiles * 128, dtype=torch.long, device=blk.device)
+    b[:n] = blk
+    b[n:] = blk[n - 1]  # padding rows reuse a slot of the tile
+    b = b.view(tiles, 128)
+    srt = b.sort(dim=1).values
+    new = torch.ones_like(srt, dtype=torch.long)
+    new[:, 1:] = (srt[:, 1:] != srt[:, :-1]).long()
+    rank = new.cumsum(1) - 1  # slot of each distinct block, in ascending block order
+    sel = torch.gather(rank, 1, torch.searchsorted(srt, b))
+    if int(sel.max()) >= 8:
+        raise ValueError("a 128-row tile holds rows of more than 8 canonical scale blocks")
+    slot_blk = b[:, :1].repeat(1, 8)
+    slot_blk.scatter_(1, sel, b)
+    used = torch.zeros(tiles, 8, dtype=torch.bool, device=blk.device)
+    used.scatter_(1, sel, True)
+    sc = scales.to(blk.device, torch.float32)[:, kb0:kb1]
+    tab = sc[slot_blk] * used.unsqueeze(-1)  # [tiles, 8, nkb]
+    tab = tab.transpose(1, 2).contiguous()  # [tiles, nkb, 8]
+    return torch.cat([sel.to(torch.uint8), tab.view(tiles, -1).view(torch.uint8)], dim=1).contiguous()
+
+
 def shard(m, rows=None, k=None, device="cuda"):
     """rank projection of canonical m: rows (LongTensor of canonical rows; None = all), k = (k0, k1) K range.
-    Every 16-row tile may hold rows of at most two 128-row scale blocks, split by r % 4 < 2 / >= 2 (true for the
-    shards of this model: head / column ranges are 16-aligned, gate|up interleaves pairs)."""
+    Every 128-row tile may hold rows of at most 8 canonical 128-row scale blocks (the shards of this model hold
+    at most 4: head / column slices, gate|up interleaved pairs)."""
     q, sc = m.q, m.scales
     N, K = q.shape
     rows = torch.arange(N) if rows is None else rows
@@ -142,20 +170,9 @@ def shard(m, rows=None, k=None, device="cuda"):
     assert k0 % 128 == 0 and k1 % 128 == 0
     rows_d = rows.to(q.device)
     ql = q.index_select(0, rows_d)[:, k0:k1].contiguous().to(device)
-    n = len(rows)
-    rows_pad = (n + 15) // 16 * 16
-    blk = torch.empty(rows_pad, dtype=torch.long)
-    blk[:n] = rows // 128  # canonical scale row of every local row
-    blk[n:] = blk[n - 1]
-    tb = blk.view(-1, 4, 4)  # [tiles, quad, row in quad]
-    sa, sb = tb[:, :, :2].reshape(-1, 8), tb[:, :, 2:].reshape(-1, 8)
-    if not (bool((sa == sa[:, :1]).all()) and bool((sb == sb[:, :1]).all())):
-        raise ValueError("a 16-row tile mixes more than two scale blocks")
-    kb0, kb1 = k0 // 128, k1 // 128
-    scd = sc.to(device, torch.float32)
-    us = torch.stack([scd[sa[:, 0].to(device)][:, kb0:kb1], scd[sb[:, 0].to(device)][:, kb0:kb1]], dim=-1)
+    table = scale_table(rows.to(device) // 128, sc, k0 // 128, k1 // 128)
     data = _lib.tile_weight(ql)
-    return GemvWeight(data=data, uscale=us.contiguous(), rows=n, K=k1 - k0)
+    return GemvWeight(data=data, uscale=table, rows=len(rows), K=k1 - k0)
 
 
 def stack_matrices(a, b):
