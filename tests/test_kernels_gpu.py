@@ -4,8 +4,9 @@ Tolerances: FP8 quantisation, weight tiling, paged-KV indexing and top-k / argma
 outputs (projections, mixer outputs) may differ from the oracle by one bf16 rounding where fp32 summation order
 moves a value across a rounding boundary: at most 2% of the elements differ, each by at most one bf16 ulp of
 its magnitude plus 1e-3 of the vector's largest magnitude (values near zero carry the fp32 sum's absolute
-error), and the largest absolute error stays under 2e-2 (BASELINE: bf16 activations within atol 2e-2). fp32
-outputs (residual updates, the GDN state) match to a relative error of 1e-5.
+error), and every element below magnitude 4 -- where one bf16 ulp is at most 2^-6 -- within an absolute 2e-2
+(bf16 activations within atol 2e-2; above 4 a single rounding flip is 2^-5 or more, which only the ulp bound
+can state). fp32 outputs (residual updates, the GDN state) match to a relative error of 1e-5.
 
 Every device argument is held in a variable until the kernel has run: a temporary's memory returns to torch's
 caching allocator at once and would be handed to the next tensor.
@@ -37,7 +38,7 @@ def bf16_close(got, ref, frac=2e-2, atol=2e-2):
     ulp = 2.0 ** (torch.floor(torch.log2(r.abs().clamp(min=1e-30))) - 7)  # one bf16 ulp at |r|
     bound = ulp + 1e-3 * r.abs().max()
     f = float((g != r).float().mean())
-    err = float(diff.max())
+    err = float(diff[r.abs() < 4].max()) if bool((r.abs() < 4).any()) else 0.0
     worst = float((diff / bound).max())
     assert f <= frac and worst <= 1.0 and err <= atol, (f, worst, err)
 
@@ -55,8 +56,8 @@ def test_quantize_bitexact(cuda):
 
 
 def test_tile_layout_bitexact(cuda):
-    """128-row tiles of 16 KB units; inside a unit the 8-row x 16-byte core matrices of the tensor core:
-    byte (r, c) at (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16"""
+    """128-row tiles of 16 KB units; inside a unit the tensor core's 128-byte-swizzled K-major rows: byte (r, c)
+    at r * 128 + ((c / 16) ^ (r % 8)) * 16 + c % 16"""
     g = torch.Generator().manual_seed(1)
     for rows, K in ((10, 640), (200, 768), (5, 2176), (257, 128)):
         q = torch.randint(0, 255, (rows, K), generator=g, dtype=torch.uint8)
@@ -65,7 +66,10 @@ def test_tile_layout_bitexact(cuda):
         rows_pad = (rows + 127) // 128 * 128
         qp = torch.zeros(rows_pad, K, dtype=torch.uint8)
         qp[:rows] = q
-        ref = qp.view(rows_pad // 128, 16, 8, K // 128, 8, 16).permute(0, 3, 1, 4, 2, 5).reshape(-1)
+        units = qp.view(rows_pad // 128, 128, K // 128, 8, 16).permute(0, 2, 1, 3, 4)  # [T, kb, r, chunk, 16]
+        r = torch.arange(128).view(128, 1)
+        src_chunk = torch.arange(8).view(1, 8) ^ (r % 8)  # stored chunk position c' holds chunk c' ^ (r % 8)
+        ref = units[:, :, torch.arange(128).view(128, 1), src_chunk].reshape(-1)
         assert torch.equal(t, ref)
 
 

@@ -267,15 +267,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         for (int jj = 0; jj < kMaxGroup; ++jj)
             if (jj == j) part[j * (2 + kHD) + 2 + tid] = o[jj];
     }
-    __threadfence();
+    // release / acquire through one thread: the barrier orders every thread's stores before thread 0's fence
+    // (cumulative) and atomic; the last CTA's fence before the barrier orders the other CTAs' parts before its
+    // threads' reads (a fence in every thread costs microseconds)
     __syncthreads();
     if (tid == 0) {
+        __threadfence();
         const int t = atomicAdd(p.ticket + b * p.nkv + g, 1);
         last_flag = (t == p.nchunks - 1);
+        if (last_flag) __threadfence();
     }
     __syncthreads();
     if (!last_flag) return;
-    __threadfence();
     // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate. The chunk
     // weights are computed once in shared memory; every thread then sums its dimension over the chunks with
     // independent loads.

@@ -16,9 +16,10 @@
 // weight scale times 2^(E-7).
 //
 // Layout (qres_tile_weight): rows in tiles of 128 (zero-padded), a tile's K in 128-wide units of 16 KB stored
-// back to back; inside a unit the canonical no-swizzle K-major arrangement of the tensor core: byte (r, c) at
-// (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16, i.e. 8-row x 16-byte core matrices, K-adjacent ones
-// 128 bytes apart (leading offset), row-adjacent ones 1024 bytes apart (stride offset). The scale table gives
+// back to back; inside a unit the tensor core's 128-byte-swizzled K-major arrangement: row r's 128 bytes at
+// r * 128, its 16-byte chunk c stored at chunk position c ^ (r % 8) (8-row groups 1024 bytes apart, the stride
+// offset; bank-conflict-free reads of any 32-byte K slice). MMA m of a unit starts 32 * m bytes into the
+// stage, inside the swizzle atom, as the hardware applies the XOR to the address bits. The scale table gives
 // each tile 128 bytes of row selectors (which of the tile's <= 8 canonical 128-row blocks holds the row) and
 // 8 fp32 scales per unit (the blocks' scales at that K block).
 //
@@ -44,7 +45,6 @@ enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3 };
 constexpr int kGemvThreads = 256;
 constexpr int kTileRows = 128;
 constexpr int kUnitBytes = 128 * 128;  // one 128-row x 128-K block of e4m3
-constexpr int kActKb = 1024;           // one user group's operand per 128-K block: 8 columns x 128 bytes
 constexpr int kDSlots = 4;             // TMEM accumulator slots, 16 fp32 columns each
 constexpr int kTmemCols = 64;
 constexpr int kMaxStages = 8;
@@ -77,7 +77,13 @@ struct GemvParams {
     uint32_t* err;
 };
 
-__host__ __device__ inline size_t gemv_act_bytes(int B, int nkw) { return (size_t)(B > 4 ? 2 : 1) * nkw * kActKb; }
+// The activations' operand, per user group of 4 (columns 2b, 2b + 1 = user b's hi, lo) and 128-K block: 8
+// K-chunks of 16 bytes, chunk j's 8 column rows at j * LBO. With B < 4 users only rows 0 .. 2B-1 are real and
+// LBO = 32 B: rows 2B..7 of a chunk are the next chunks' real rows, read by the MMA into D columns nobody reads
+// (a column of D depends only on its own operand column), which shrinks the operand 4x at one user.
+__host__ __device__ constexpr int gemv_act_lbo(int B) { return B >= 4 ? 128 : 32 * B; }
+__host__ __device__ inline size_t gemv_act_group(int B, int nkw) { return (size_t)nkw * 8 * gemv_act_lbo(B) + 128; }
+__host__ __device__ inline size_t gemv_act_bytes(int B, int nkw) { return (size_t)(B > 4 ? 2 : 1) * gemv_act_group(B, nkw); }
 __host__ __device__ inline size_t gemv_ainv_bytes(int nkw) { return ((size_t)nkw * 8 * 4 + 127) & ~size_t(127); }
 __host__ __device__ inline size_t gemv_smem_bytes(int B, int nkw, int nstages) {
     const size_t pre = kHeadBytes + gemv_ainv_bytes(nkw) + gemv_act_bytes(B, nkw);
@@ -86,10 +92,11 @@ __host__ __device__ inline size_t gemv_smem_bytes(int B, int nkw, int nstages) {
 
 // ---- tcgen05 wrappers (cta_group::1) ------------------------------------------------------------------------
 
-// shared-memory matrix descriptor, no swizzle: start, leading (K) and stride (M/N) byte offsets, version 1
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// shared-memory matrix descriptor: start, leading (K) and stride (M/N) byte offsets, version 1, layout type
+// (bits 61-63: 0 no swizzle, 2 = 128-byte swizzle; a swizzled operand's atoms are 1024-byte aligned)
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout = 0) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
 __device__ __forceinline__ void tc_mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
@@ -201,11 +208,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     uint64_t* dempty = dfull + kDSlots;                  // [kDSlots] accumulator slot read (4 epilogue warps)
     uint64_t* drain = dempty + kDSlots;                  // every MMA of the CTA completed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-    int* tk_slot = reinterpret_cast<int*>(tmem_slot + 1);
+    int* tk_slot = reinterpret_cast<int*>(tmem_slot + 1);  // [2]
     float (*red)[8] = reinterpret_cast<float (*)[8]>(smem + 512);  // [8 warps][8 users]
     const int nkw = p.nkw;
     float* ainv = reinterpret_cast<float*>(smem + kHeadBytes);  // [nkw][8]: 2^(E-7) per K block and user
-    uint8_t* act = smem + kHeadBytes + gemv_ainv_bytes(nkw);   // [group][nkw][8 chunks][8 columns][16 bytes]
+    uint8_t* act = smem + kHeadBytes + gemv_ainv_bytes(nkw);   // [group][nkw][8 chunks x LBO] (+ tail)
+    constexpr int LBO = gemv_act_lbo(B);
+    const size_t gstride = gemv_act_group(B, nkw);
     const size_t pre = kHeadBytes + gemv_ainv_bytes(nkw) + gemv_act_bytes(B, nkw);
     uint8_t* ring = smem + ((pre + 1023) & ~size_t(1023));
 
@@ -251,30 +260,78 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     pdl_wait();
     const int users = p.users;
 
-    // ---- prologue: the activations' hi / lo operand for the K blocks of this CTA's window
-    for (int i = tid; i < (int)(gemv_act_bytes(B, nkw) / 16); i += kGemvThreads)
-        reinterpret_cast<uint4*>(act)[i] = make_uint4(0, 0, 0, 0);
+    // ---- prologue: the activations' hi / lo operand for the K blocks of this CTA's window. Columns of users
+    // past B (B < 4) are never written: an MMA column depends on its own operand column only.
+    //
+    // put_operand: the warp's 128 values h of user b, K block at window slot ws (lane: positions 4 lane .. + 3)
+    // -> E = exponent of the block's max |h|, hi / lo e4m3 of h * 2^(7-E), 2^(E-7) for the epilogue
+    auto put_operand = [&](int b, int ws, const float* h) {
+        const float m = warp_max(fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3]))));
+        int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
+        e = max(e, -100);
+        const float f = __uint_as_float((uint32_t)(127 + 7 - e) << 23);   // 2^(7-E): max|h| * f in [128, 256)
+        const float fi = __uint_as_float((uint32_t)(127 - 7 + e) << 23);  // 2^(E-7)
+        float lo[4];
+        uint32_t hi_w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+            const float y0 = h[j] * f, y1 = h[j + 1] * f;
+            const uint32_t hb = e4m3x2(y0, y1);
+            const float2 hf = e4m3x2_f32(hb);
+            lo[j] = y0 - hf.x;  // exact
+            lo[j + 1] = y1 - hf.y;
+            hi_w |= hb << (8 * j);
+        }
+        const uint32_t lo_w = e4m3x2(lo[0], lo[1]) | (e4m3x2(lo[2], lo[3]) << 16);
+        uint8_t* dst = act + (size_t)(b >> 2) * gstride + (size_t)ws * 8 * LBO + (lane >> 2) * LBO +
+                       (2 * (b & 3)) * 16 + (lane & 3) * 4;
+        *reinterpret_cast<uint32_t*>(dst) = hi_w;
+        *reinterpret_cast<uint32_t*>(dst + 16) = lo_w;
+        if (lane == 0) ainv[ws * 8 + b] = (b < users && m > 0.f) ? fi : 0.f;
+    };
+    auto xload = [&](int b, int i) -> float4 {
+        float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
+        if (PRO == PRO_RMSNORM_ADD) {
+            const float4 r = reinterpret_cast<const float4*>(p.red + (size_t)b * K)[i];
+            v.x += r.x;
+            v.y += r.y;
+            v.z += r.z;
+            v.w += r.w;
+        }
+        return v;
+    };
+    // rmsnorm with B <= 2 rows and K <= 8192 (the hidden size): one pass over x. Thread t's float4 j is
+    // x[4 (t + 256 j) ..] -- K block warp + 8 j at lane -- so each warp writes the operand of the blocks it
+    // holds, straight from registers.
+    constexpr bool kRegs = PRO != PRO_BF16 && B <= 2;
+    constexpr int kXj = 8;
+    const bool regs = kRegs && K <= kXj * 4 * kGemvThreads;
     float rn[B];
     if (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) {
-        auto xload = [&](int b, int i) -> float4 {
-            float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
-            if (PRO == PRO_RMSNORM_ADD) {
-                const float4 r = reinterpret_cast<const float4*>(p.red + (size_t)b * K)[i];
-                v.x += r.x;
-                v.y += r.y;
-                v.z += r.z;
-                v.w += r.w;
-            }
-            return v;
-        };
+        float4 xr[kRegs ? B : 1][kXj];
 #pragma unroll
         for (int b = 0; b < B; ++b) {
             float ss = 0.f;
             if (b < users) {
-                for (int i = tid; i < K / 4; i += kGemvThreads) {
-                    const float4 v = xload(b, i);
-                    if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                if (regs) {
+#pragma unroll
+                    for (int j = 0; j < kXj; ++j) {
+                        const int i = tid + j * kGemvThreads;
+                        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (i < K / 4) {
+                            v = xload(b, i);
+                            if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
+                        }
+                        xr[kRegs ? b : 0][j] = v;
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
+                } else {
+#pragma unroll 5
+                    for (int i = tid; i < K / 4; i += kGemvThreads) {
+                        const float4 v = xload(b, i);
+                        if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
                 }
             }
             ss = warp_sum(ss);
@@ -288,68 +345,75 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             for (int w = 0; w < 8; ++w) tsum += red[w][b];
             rn[b] = rsqrt_ieee(tsum / (float)K + kEps);
         }
+        if (regs) {
+#pragma unroll
+            for (int j = 0; j < kXj; ++j) {
+                const int kb = warp + 8 * j;  // warp-uniform
+                if (kb >= nkb) break;
+                int ws = kb - kb_start;
+                if (ws < 0) ws += nkb;
+                if (ws >= nwin) continue;  // outside this CTA's window
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const float4 v = xr[kRegs ? b : 0][j];
+                    // h = bf16(x * r)
+                    const float h[4] = {bf16_round(v.x * rn[b]), bf16_round(v.y * rn[b]), bf16_round(v.z * rn[b]),
+                                        bf16_round(v.w * rn[b])};
+                    put_operand(b, ws, h);
+                }
+            }
+        }
     } else {
 #pragma unroll
         for (int b = 0; b < B; ++b) rn[b] = 1.f;
-        __syncthreads();  // the zeroed operand before the writes below
     }
-    // one warp per (user, K block): lane holds K positions 4 * lane .. + 3 of the block
-    for (int pr = warp; pr < B * nwin; pr += 8) {
-        const int b = pr % B, ws = pr / B;
-        int kb = kb_start + ws;
-        if (kb >= nkb) kb -= nkb;
-        float h[4] = {0.f, 0.f, 0.f, 0.f};
-        if (b < users) {
-            if (PRO == PRO_BF16) {
-                const uint2 v = *reinterpret_cast<const uint2*>(p.in + (size_t)b * p.ld_in + kb * 128 + 4 * lane);
-                h[0] = bf16lo(v.x);
-                h[1] = bf16hi(v.x);
-                h[2] = bf16lo(v.y);
-                h[3] = bf16hi(v.y);
-            } else {
-                const float4* xp = reinterpret_cast<const float4*>(p.x + (size_t)b * K + kb * 128) + lane;
-                float4 v = *xp;
-                if (PRO == PRO_RMSNORM_ADD) {
-                    const float4 r = reinterpret_cast<const float4*>(p.red + (size_t)b * K + kb * 128)[lane];
-                    v.x += r.x;
-                    v.y += r.y;
-                    v.z += r.z;
-                    v.w += r.w;
+    // otherwise one warp per (user, K block) pair, 4 pairs in flight: lane holds K positions 4 * lane .. + 3
+    const int npairs = regs ? 0 : B * nwin;
+    for (int pr0 = warp; pr0 < npairs; pr0 += 32) {
+        float hv[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int pr = pr0 + 8 * c;
+            const int b = pr % B, ws = pr / B;
+            int kb = kb_start + ws;
+            if (kb >= nkb) kb -= nkb;
+            hv[c][0] = hv[c][1] = hv[c][2] = hv[c][3] = 0.f;
+            if (pr < npairs && b < users) {
+                if (PRO == PRO_BF16) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(p.in + (size_t)b * p.ld_in + kb * 128 + 4 * lane);
+                    hv[c][0] = bf16lo(v.x);
+                    hv[c][1] = bf16hi(v.x);
+                    hv[c][2] = bf16lo(v.y);
+                    hv[c][3] = bf16hi(v.y);
+                } else {
+                    const float4 v = xload(b, kb * 32 + lane);
+                    hv[c][0] = v.x;
+                    hv[c][1] = v.y;
+                    hv[c][2] = v.z;
+                    hv[c][3] = v.w;
                 }
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int pr = pr0 + 8 * c;
+            if (pr >= npairs) break;  // warp-uniform
+            const int b = pr % B, ws = pr / B;
+            float h[4];
+            if (PRO == PRO_BF16) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) h[j] = hv[c][j];
+            } else {
                 // h = bf16(x * r)
                 float rb = 1.f;
 #pragma unroll
                 for (int bb = 0; bb < B; ++bb)
                     if (bb == b) rb = rn[bb];
-                h[0] = bf16_round(v.x * rb);
-                h[1] = bf16_round(v.y * rb);
-                h[2] = bf16_round(v.z * rb);
-                h[3] = bf16_round(v.w * rb);
-            }
-        }
-        const float m = warp_max(fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3]))));
-        int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
-        e = max(e, -100);
-        const float f = __uint_as_float((uint32_t)(127 + 7 - e) << 23);    // 2^(7-E): max|h| * f in [128, 256)
-        const float fi = __uint_as_float((uint32_t)(127 - 7 + e) << 23);   // 2^(E-7)
-        float y[4], lo[4];
-        uint32_t hi_w = 0;
 #pragma unroll
-        for (int j = 0; j < 4; j += 2) {
-            y[j] = h[j] * f;
-            y[j + 1] = h[j + 1] * f;
-            const uint32_t hb = e4m3x2(y[j], y[j + 1]);
-            const float2 hv = e4m3x2_f32(hb);
-            lo[j] = y[j] - hv.x;  // exact
-            lo[j + 1] = y[j + 1] - hv.y;
-            hi_w |= hb << (8 * j);
+                for (int j = 0; j < 4; ++j) h[j] = bf16_round(hv[c][j] * rb);
+            }
+            put_operand(b, ws, h);
         }
-        const uint32_t lo_w = e4m3x2(lo[0], lo[1]) | (e4m3x2(lo[2], lo[3]) << 16);
-        uint8_t* dst = act + (size_t)(b >> 2) * nkw * kActKb + (size_t)ws * kActKb + (lane >> 2) * 128 +
-                       (2 * (b & 3)) * 16 + (lane & 3) * 4;
-        *reinterpret_cast<uint32_t*>(dst) = hi_w;
-        *reinterpret_cast<uint32_t*>(dst + 16) = lo_w;
-        if (lane == 0) ainv[ws * 8 + b] = (b < users && m > 0.f) ? fi : 0.f;
     }
     fence_proxy_async();  // the operand written by generic stores, read by the tensor core (async proxy)
     tc_fence_before();
@@ -377,7 +441,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         // ---- MMA issuer
         if (lane == 0) {
             const uint32_t ring_a = smem_addr(ring), act_a = smem_addr(act);
-            const uint32_t sbo_b = B > 4 ? (uint32_t)(nkw * kActKb) : 0u;  // users 4..7 (columns 8..15)
+            const uint32_t sbo_b = B > 4 ? (uint32_t)gstride : 0u;  // users 4..7 (columns 8..15)
             int ws = 0;
             for (int i = 0; i < cnt; ++i) {
                 const int slot = i % NS, d = i % kDSlots;
@@ -386,8 +450,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                 tc_fence_after();
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
-                    const uint64_t ad = smem_desc(ring_a + slot * kUnitBytes + m * 256, 128, 1024);
-                    const uint64_t bd = smem_desc(act_a + ws * kActKb + m * 256, 128, sbo_b);
+                    const uint64_t ad = smem_desc(ring_a + slot * kUnitBytes + m * 32, 16, 1024, 2);
+                    const uint64_t bd = smem_desc(act_a + ws * 8 * LBO + m * 2 * LBO, LBO, sbo_b);
                     tc_mma_f8(tmem + d * 16, ad, bd, m > 0 ? 1u : 0u);
                 }
                 tc_commit(&empty[slot]);
@@ -408,30 +472,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         int cur = -1, first_tile = -1;
         const int first_T = u0 / nkb;
         auto split_tile = [&](int T) { return cta_of_unit(T * nkb, base, rem) != cta_of_unit(T * nkb + nkb - 1, base, rem); };
-        auto flush = [&](int T, float* v) {
-            const int c0 = cta_of_unit(T * nkb, base, rem), c1 = cta_of_unit(T * nkb + nkb - 1, base, rem);
-            if (c0 != c1) {
-                const int slot = (T == first_T) ? 0 : 1;
-                float* dst = p.part + ((size_t)blockIdx.x * 2 + slot) * 8 * 128;
-#pragma unroll
-                for (int b = 0; b < B; ++b) dst[b * 128 + row] = v[b];
-                __threadfence();
-                bar_sync(1, 128);
-                if (row == 0) *tk_slot = atomicAdd(p.ticket + T, 1);
-                bar_sync(1, 128);
-                if (*tk_slot != c1 - c0) return;
-                __threadfence();
-#pragma unroll
-                for (int b = 0; b < B; ++b) v[b] = 0.f;
-                for (int c = c0; c <= c1; ++c) {
-                    const int cu0 = c * base + min(c, rem);
-                    const int sl = (T == cu0 / nkb) ? 0 : 1;
-                    const float* src = p.part + ((size_t)c * 2 + sl) * 8 * 128;
-#pragma unroll
-                    for (int b = 0; b < B; ++b) v[b] += __ldcg(src + b * 128 + row);
-                }
-                if (row == 0) p.ticket[T] = 0;
-            }
+        auto store = [&](int T, const float* v) {
             const int r = T * kTileRows + row;
             if (EPI == EPI_SILU_MUL) {
                 // quads of rows are gate(j), gate(j+1), up(j), up(j+1): the up partner of row r is r + 2
@@ -459,6 +500,66 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                         reinterpret_cast<float*>(p.out)[(size_t)b * p.ld_out + r] = v[b];
                     }
                 }
+            }
+        };
+        // the tiles of this CTA split with other CTAs (only its first and its last tile can be), finished
+        // together in one round: parts out, one ticket each, the last CTA of a tile adds the parts in CTA order
+        auto finish_split = [&](int n, int T0, float* v0, int T1, float* v1) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                if (t >= n) break;
+                const int T = t ? T1 : T0;
+                const float* v = t ? v1 : v0;
+                float* dst = p.part + ((size_t)blockIdx.x * 2 + (T == first_T ? 0 : 1)) * 8 * 128;
+#pragma unroll
+                for (int b = 0; b < B; ++b) dst[b * 128 + row] = v[b];
+            }
+            // release / acquire through one thread per tile: the named barrier orders every epilogue thread's
+            // part stores before that thread's (cumulative) fence and ticket; the last CTA of a tile fences again
+            // before the barrier that releases its threads' reads (a fence in every thread costs microseconds)
+            bar_sync(1, 128);
+            if (row < n) {
+                __threadfence();
+                const int T = row ? T1 : T0;
+                const int tk = atomicAdd(p.ticket + T, 1);
+                tk_slot[row] = tk;
+                if (tk == cta_of_unit(T * nkb + nkb - 1, base, rem) - cta_of_unit(T * nkb, base, rem)) __threadfence();
+            }
+            bar_sync(1, 128);
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                if (t >= n) break;
+                const int T = t ? T1 : T0;
+                float* v = t ? v1 : v0;
+                const int c0 = cta_of_unit(T * nkb, base, rem), c1 = cta_of_unit(T * nkb + nkb - 1, base, rem);
+                if (tk_slot[t] != c1 - c0) continue;  // uniform over the epilogue warps
+                // the parts of up to 16 CTAs in flight at once (one L2 round trip per batch: the loads are
+                // unconditional, past-the-end ones re-read the last part), added in CTA order
+                constexpr int kBatch = B <= 2 ? 16 : B <= 4 ? 8 : 4;
+#pragma unroll
+                for (int b = 0; b < B; ++b) v[b] = 0.f;
+                for (int c = c0; c <= c1; c += kBatch) {
+                    const float* src[kBatch];
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j) {
+                        const int cc = min(c + j, c1);
+                        const int cu0 = cc * base + min(cc, rem);
+                        src[j] = p.part + ((size_t)cc * 2 + ((T == cu0 / nkb) ? 0 : 1)) * 8 * 128 + row;
+                    }
+                    float q[kBatch][B];
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j)
+#pragma unroll
+                        for (int b = 0; b < B; ++b) q[j][b] = __ldcg(src[j] + b * 128);
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j)
+                        if (c + j <= c1) {
+#pragma unroll
+                            for (int b = 0; b < B; ++b) v[b] += q[j][b];
+                        }
+                }
+                if (row == 0) p.ticket[T] = 0;
+                store(T, v);
             }
         };
 
@@ -491,12 +592,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             if (lane == 0) mbar_arrive(&dempty[d]);
             if (Tc != cur) {
                 if (cur >= 0) {
-                    if (first_tile < 0 && cur == first_T && split_tile(cur)) {
+                    // a tile that ends inside the range: the first one may be split (held for the end), any
+                    // later one lies wholly in this CTA
+                    if (cur == first_T && split_tile(cur)) {
                         first_tile = cur;
 #pragma unroll
                         for (int b = 0; b < B; ++b) first_acc[b] = acc[b];
                     } else {
-                        flush(cur, acc);
+                        store(cur, acc);
                     }
                 }
 #pragma unroll
@@ -506,8 +609,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = fmaf(v[2 * b] + v[2 * b + 1], s * ainv[wsc * 8 + b], acc[b]);
         }
-        if (cur >= 0) flush(cur, acc);
-        if (first_tile >= 0) flush(first_tile, first_acc);
+        if (cur >= 0 && !split_tile(cur)) {
+            store(cur, acc);
+            cur = -1;
+        }
+        if (cur >= 0 && first_tile >= 0) finish_split(2, first_tile, first_acc, cur, acc);
+        else if (cur >= 0) finish_split(1, cur, acc, 0, acc);
+        else if (first_tile >= 0) finish_split(1, first_tile, first_acc, 0, first_acc);
     }
     if (warp == 0 && lane == 0) {
         // never release shared memory with a copy still landing in it
@@ -559,7 +667,10 @@ static cudaError_t launch_pe(const GemvParams& p, int Bt, int grid, size_t smem,
 // shared memory of one GEMV CTA: half an SM's (a second CTA -- the next projection's, under programmatic
 // dependent launch -- fits beside it and starts its weight stream during this one's tail); past that, up to
 // the per-CTA maximum with a shallower ring
-constexpr size_t kGemvSmemBudget = 113 * 1024;
+#ifndef QRES_GEMV_BUDGET_KB
+#define QRES_GEMV_BUDGET_KB 113
+#endif
+constexpr size_t kGemvSmemBudget = QRES_GEMV_BUDGET_KB * 1024;
 constexpr size_t kGemvSmemMax = 227 * 1024;
 constexpr int kMinStages = 3;
 

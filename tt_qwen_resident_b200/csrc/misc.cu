@@ -12,9 +12,9 @@
 namespace qres {
 
 // ------------------------------------------------------------------------------------------------ tiling
-// 128-row tiles, 128-K units of 16 KB back to back per tile, inside a unit the tensor core's no-swizzle K-major
-// core matrices: dst[(T * nkb + kb) * 16384 + (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16] =
-// src[(128 T + r) * K + 128 kb + c], zero past the last row. One thread per 16-byte granule (one core-matrix row).
+// 128-row tiles, 128-K units of 16 KB back to back per tile, inside a unit the tensor core's 128-byte-swizzled
+// K-major rows: dst[(T * nkb + kb) * 16384 + r * 128 + ((c / 16) ^ (r % 8)) * 16 + c % 16] =
+// src[(128 T + r) * K + 128 kb + c], zero past the last row. One thread per 16-byte granule.
 __global__ void tile_weight_kernel(const uint8_t* __restrict__ src, int rows, int K, uint8_t* __restrict__ dst,
                                    size_t total16) {
     const int nkb = K / 128;
@@ -24,7 +24,7 @@ __global__ void tile_weight_kernel(const uint8_t* __restrict__ src, int rows, in
         const int inner = (int)(off % 16384);
         const size_t T = unit / nkb;
         const int kb = (int)(unit % nkb);
-        const int r = (inner / 1024) * 8 + (inner % 128) / 16, c = ((inner % 1024) / 128) * 16;
+        const int r = inner / 128, c = (((inner % 128) / 16) ^ (r % 8)) * 16;
         const size_t row = T * 128 + r;
         uint4 val = make_uint4(0, 0, 0, 0);
         if (row < (size_t)rows) val = *reinterpret_cast<const uint4*>(src + row * K + (size_t)kb * 128 + c);
@@ -208,12 +208,15 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const TopkParams p) 
     __syncthreads();
     uint32_t* mine = p.cand + ((size_t)row * p.nblk + blk) * 2 * kTopK;
     block_top32(keys, idx, cnt, mine, mine + kTopK, hist, scratch);
-    __threadfence();
+    // release / acquire through one thread (barrier, then thread 0's cumulative fence and atomic)
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(p.ticket + row, 1) == p.nblk - 1;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(p.ticket + row, 1) == p.nblk - 1;
+        if (last) __threadfence();
+    }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     // merge: the candidates of every block, in block order (indices ascend with block, then rank in list)
     const uint32_t* all = p.cand + (size_t)row * p.nblk * 2 * kTopK;
     int m = 0;
