@@ -350,7 +350,10 @@ def run_ours(args, rank, world, local):
                 "unit": "GB/s",
                 "frac": gemv_gbs / peak,
                 "peak_kind": peak_kind,
-                "traffic": None,
+                # dram__bytes_read.sum + dram__bytes_write.sum of this kernel at this shape, from the committed
+                # ncu capture (profiles/gemv_fp8_gateup_34816x5120_b1.md): 178.76 MB + 3.97 MB
+                "traffic": 182731008 if (batch == 1 and world == 1) else None,
+                "traffic_source": "ncu --set full, profiles/gemv_fp8_gateup_34816x5120_b1.md" if (batch == 1 and world == 1) else None,
                 "bytes_per_launch": gw.nbytes,
                 "ms_per_launch": gemv_ms,
             },
