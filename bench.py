@@ -17,6 +17,7 @@ Arms:
              step a bounded sample (4 layers G G G A + the lm_head, extrapolated to 64 layers); rank 0 only.
 """
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -42,6 +43,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="tensor-parallel exchange: the fused NVLink peer exchange (default) or NCCL (baseline)")
     return ap.parse_args()
 
 
@@ -214,10 +217,13 @@ def run_ours(args, rank, world, local):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
-        obj = [nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nid = obj[0]
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        if args.exchange == "nccl":
+            obj = [nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            nid = obj[0]
+        else:
+            nid = None
     else:
         nid = None
 
@@ -229,7 +235,7 @@ def run_ours(args, rank, world, local):
     w = weights.random_canonical(layers, INTERVAL, VOCAB, seed=0, device=dev)
     emb = torch.randn(VOCAB, 5120, generator=torch.Generator(device=dev).manual_seed(1), device=dev).bfloat16()
     model = ResidentModel(w, layers, INTERVAL, batch=batch, max_pos=max_pos, lm_head=True, embed=emb, rank=rank,
-                          nranks=world, nccl_id=nid, device=dev)
+                          nranks=world, nccl_id=nid, p2p=world > 1 and args.exchange == "p2p", device=dev)
     del w
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t_build
@@ -333,6 +339,8 @@ def run_ours(args, rank, world, local):
                 "prompt": prompt,
                 "layers": layers,
                 "parallelism": f"tp{world}",
+                "exchange": ("fused NVLink peer exchange in the GEMV epilogue" if args.exchange == "p2p" else "NCCL")
+                if world > 1 else None,
                 "l2": "inputs larger than L2 (25.6 GB of weights streamed per step)",
             },
             "e2e": {

@@ -144,6 +144,22 @@ QRES_API qres_status qres_bind_workspace(qres_ctx* ctx, void* dev, size_t bytes)
 QRES_API qres_status qres_nccl_unique_id(const char* libpath, void* id128);
 QRES_API qres_status qres_nccl_init(qres_ctx* ctx, const char* libpath, const void* id128);
 
+/* ---- fused tensor-parallel exchange over NVLink peer memory ----
+ * Replaces the NCCL path above inside the step (mlp_hub.cpp:309-364 all-reduce, :366-411 list exchange): the
+ * row-parallel out- / down-projection stores each finished 128-row tile of its fp32 partial straight into every
+ * rank's window from its epilogue (peer stores) and advances a counter there; the next projection's rmsnorm
+ * prologue waits for all ranks' counters (bounded; a timeout sets the device error word) and adds the partials in
+ * rank order, so every rank holds the same residual bit for bit. The lm_head's top-32 lists travel the same way.
+ * Bytes of this rank's window: */
+QRES_API qres_status qres_p2p_window_size(const qres_ctx* ctx, size_t* bytes);
+/* Allocate this rank's window (cudaMalloc, zeroed -- the one device allocation the library makes itself, since
+ * CUDA IPC maps whole allocations; freed by qres_destroy) and write its CUDA IPC handle (64 bytes). */
+QRES_API qres_status qres_p2p_alloc(qres_ctx* ctx, void* handle64);
+/* Map every rank's window (nranks handles of 64 bytes in rank order, as all-gathered by the caller) and switch
+ * the step to the peer exchange. Needs the workspace bound; resets the device step count the exchange counters
+ * derive from, so every rank opens before any rank's first step (a barrier after the call). */
+QRES_API qres_status qres_p2p_open(qres_ctx* ctx, const void* handles);
+
 /* ---- the step (ResidentModel.step, model.py:1499-1508) ---- */
 /* Enqueue one decode step on `stream`. */
 QRES_API qres_status qres_decode_step(qres_ctx* ctx, void* stream);

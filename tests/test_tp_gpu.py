@@ -1,8 +1,15 @@
-"""Tensor parallelism on 2 GPUs: each rank runs ResidentModel on its shard (heads, MLP columns, vocab), the
-out- and down-projection partials are all-reduced over NCCL, the lm_head's per-rank top-32 lists are gathered
-and merged. The result must match the oracle run at n = 2 from the same state (x and each rank's logits within
-2e-2 relative, the greedy pick by the argmax rule over the gathered logits), and both ranks must hold the same x
-bit for bit. Skipped with fewer than 2 GPUs."""
+"""Tensor parallelism on 2 GPUs: each rank runs ResidentModel on its shard (heads, MLP columns, vocab); the out- and
+down-projection partials are summed across ranks and the lm_head's per-rank top-32 lists are merged. Two
+exchanges are compared:
+- NCCL (the baseline): the GEMV writes its fp32 partial, ncclAllReduce sums it, the next GEMV's prologue adds it;
+- the fused peer exchange (qres_p2p_*): the GEMV epilogue stores each finished tile into both ranks' windows over
+  NVLink and the next GEMV's prologue waits for both ranks' counters and adds the partials in rank order.
+At n = 2 both form p0 + p1 and add it to x, so the two modes must agree bit for bit over an eager step and three
+CUDA-graph replays (which also exercises the exchange counters across steps). The first step must match the
+oracle run at n = 2 from the same state (x and each rank's logits within 2e-2 relative, the greedy pick by the
+argmax rule over the gathered logits), and both ranks must hold the same x bit for bit. Skipped with fewer than
+2 GPUs.
+"""
 import os
 
 import pytest
@@ -11,6 +18,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
+
+STEPS = 4  # one eager step, then three graph replays
 
 
 def _rank(rank, world, port, w8, out):
@@ -26,26 +35,29 @@ def _rank(rank, world, port, w8, out):
     dist.broadcast_object_list(obj, src=0)
     dev = torch.device("cuda", rank)
     st = refgen.random_state(3, 1, 70, 134, seed=1)
-    model = ResidentModel(weights.canonical_from_fp8(w8, device=dev), 4, 4, batch=1, max_pos=134, lm_head=True,
-                          rank=rank, nranks=world, nccl_id=obj[0], device=dev)
-    model.load_state(st)
     x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
-    for trace in (False, True):
-        if trace:
-            model.load_state(st)
-            model.capture_trace()
-        model.step(model.token_state(x0, st.pos))
-        model.check()
-        out[(rank, trace)] = (model.x().clone(), model.logits().clone(), model.argmax())
-    model.close()
-    dist.barrier()
+    for mode in ("nccl", "p2p"):
+        model = ResidentModel(weights.canonical_from_fp8(w8, device=dev), 4, 4, batch=1, max_pos=134, lm_head=True,
+                              rank=rank, nranks=world, nccl_id=obj[0] if mode == "nccl" else None,
+                              p2p=mode == "p2p", device=dev)
+        model.load_state(st)
+        res = []
+        for k in range(STEPS):
+            if k == 1:
+                model.capture_trace()
+            model.step(model.token_state(x0, st.pos + k))
+            model.check()
+            res.append((model.x().clone(), model.logits().clone(), model.argmax()))
+        out[(rank, mode)] = res
+        model.close()
+        dist.barrier()
     dist.destroy_process_group()
 
 
-def test_tp2_decode_step_matches_oracle():
+def test_tp2_decode_step_matches_oracle_nccl_and_peer_exchange():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    from oracle import fp8, refgen, sampling, step
+    from oracle import refgen, sampling, step
     from test_model_gpu import dequantized, quantized
 
     torch.set_num_threads(8)
@@ -60,12 +72,17 @@ def test_tp2_decode_step_matches_oracle():
     x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
     x_ref, lg = step.torch_step(x0, P, st, 4, 4, lm_head=True)
     rel = lambda a, b: float((a - b).norm() / b.norm())
-    for trace in (False, True):
-        x0_, l0, a0 = out[(0, trace)]
-        x1_, l1, a1 = out[(1, trace)]
-        assert torch.equal(x0_, x1_)
-        assert rel(x0_, x_ref) < 2e-2
-        assert rel(l0, step.logits_bf16([lg[0]])) < 2e-2 and rel(l1, step.logits_bf16([lg[1]])) < 2e-2
-        got = torch.cat([l0, l1])
-        assert a0 == a1 == sampling.argmax_rule(got)
-    assert torch.equal(out[(0, False)][0], out[(0, True)][0])  # graph replay == eager
+    for mode in ("nccl", "p2p"):
+        x0_, l0, a0 = out[(0, mode)][0]
+        x1_, l1, a1 = out[(1, mode)][0]
+        assert rel(x0_, x_ref) < 2e-2, mode
+        assert rel(l0, step.logits_bf16([lg[0]])) < 2e-2 and rel(l1, step.logits_bf16([lg[1]])) < 2e-2, mode
+        assert a0 == a1 == sampling.argmax_rule(torch.cat([l0, l1])), mode
+    for k in range(STEPS):
+        for r in range(world):
+            xn, ln, an = out[(r, "nccl")][k]
+            xp, lp, ap = out[(r, "p2p")][k]
+            assert torch.equal(xn, xp), (k, r)  # the fused exchange reproduces the NCCL sum bit for bit
+            assert torch.equal(ln, lp) and an == ap, (k, r)
+        for mode in ("nccl", "p2p"):
+            assert torch.equal(out[(0, mode)][k][0], out[(1, mode)][k][0]), (k, mode)  # ranks agree

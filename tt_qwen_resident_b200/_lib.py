@@ -33,6 +33,9 @@ EXPORTS = [
     "qres_bind_workspace",
     "qres_nccl_unique_id",
     "qres_nccl_init",
+    "qres_p2p_window_size",
+    "qres_p2p_alloc",
+    "qres_p2p_open",
     "qres_decode_step",
     "qres_capture",
     "qres_replay",
@@ -131,6 +134,9 @@ def lib():
             "qres_bind_workspace": [vp, vp, sz],
             "qres_nccl_unique_id": [ctypes.c_char_p, vp],
             "qres_nccl_init": [vp, ctypes.c_char_p, vp],
+            "qres_p2p_window_size": [vp, ctypes.POINTER(sz)],
+            "qres_p2p_alloc": [vp, vp],
+            "qres_p2p_open": [vp, vp],
             "qres_decode_step": [vp, vp],
             "qres_capture": [vp, vp],
             "qres_replay": [vp, vp],

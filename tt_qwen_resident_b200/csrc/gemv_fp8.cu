@@ -40,7 +40,8 @@
 namespace qres {
 
 enum { PRO_RMSNORM = 0, PRO_BF16 = 1, PRO_RMSNORM_ADD = 2 };
-enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3 };
+enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3, EPI_P2P = 4 };
+constexpr int kMaxPeers = 8;
 
 constexpr int kGemvThreads = 256;
 constexpr int kTileRows = 128;
@@ -61,8 +62,19 @@ struct GemvParams {
     int rows, tiles, K, nkb;
     int users;              // real users (<= template B)
     const float* x;         // PRO_RMSNORM(_ADD): fp32 [users][K]
-    const float* red;       // PRO_RMSNORM_ADD: all-reduced partials [users][K]; x_out = x + red
+    const float* red;       // PRO_RMSNORM_ADD: partials [nsrc][users][K]; x_out = x + (sum of the sources in order)
     float* x_out;           // PRO_RMSNORM_ADD: written by CTA 0
+    int nsrc;               // PRO_RMSNORM_ADD: 1 (all-reduced by NCCL) or one per rank (peer exchange)
+    size_t src_stride;      // fp32 sources: floats between two sources
+    // PRO_RMSNORM_ADD over the peer exchange: the sources are tagged words [nsrc][users][K], read until every word
+    // carries this exchange's tag (*epoch * tag_mul + tag_add)
+    const uint2* tagged;
+    const uint32_t* epoch;
+    uint32_t tag_mul, tag_add;
+    // EPI_P2P: every finished row goes to each rank's window (this rank's region, [user][peer_ld]) as a tagged word
+    int p2p_n;
+    int peer_ld;
+    uint2* peer_data[kMaxPeers];
     const uint16_t* in;     // PRO_BF16: bf16 [users][ld_in]
     int ld_in;
     void* out;              // EPI_BF16 / EPI_SILU_MUL: bf16 [users][ld_out]; EPI_RESID / EPI_F32: fp32
@@ -289,10 +301,44 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         *reinterpret_cast<uint32_t*>(dst + 16) = lo_w;
         if (lane == 0) ainv[ws * 8 + b] = (b < users && m > 0.f) ? fi : 0.f;
     };
+    // the tag of this launch's peer exchange (PRO_RMSNORM_ADD over tagged sources, or EPI_P2P)
+    const uint32_t tag = (p.tagged != nullptr || EPI == EPI_P2P) ? *p.epoch * p.tag_mul + p.tag_add : 0u;
+    // 4 consecutive tagged words of a source: re-read (bounded) until all carry the tag
+    auto tagged4 = [&](const uint2* src) -> float4 {
+        for (uint32_t it = 0;; ++it) {
+            const uint4 a = ld_volatile128(src), c = ld_volatile128(src + 2);
+            const bool fresh = a.y == tag && a.w == tag && c.y == tag && c.w == tag;
+            if (fresh || it >= kPeerSpinLimit) {
+                if (!fresh) atomicOr(p.err, kErrPeer | kErrTimeout);
+                return make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(c.x), __uint_as_float(c.z));
+            }
+            __nanosleep(32);
+        }
+    };
     auto xload = [&](int b, int i) -> float4 {
         float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
         if (PRO == PRO_RMSNORM_ADD) {
-            const float4 r = reinterpret_cast<const float4*>(p.red + (size_t)b * K)[i];
+            // the sources summed in rank order first (n = 2: the same sum NCCL forms), then added to x
+            float4 r;
+            if (p.tagged != nullptr) {
+                r = tagged4(p.tagged + (size_t)b * K + 4 * i);
+                for (int s = 1; s < p.nsrc; ++s) {
+                    const float4 q = tagged4(p.tagged + ((size_t)s * p.users + b) * K + 4 * i);
+                    r.x += q.x;
+                    r.y += q.y;
+                    r.z += q.z;
+                    r.w += q.w;
+                }
+            } else {
+                r = __ldcg(reinterpret_cast<const float4*>(p.red + (size_t)b * K) + i);
+                for (int s = 1; s < p.nsrc; ++s) {
+                    const float4 q = __ldcg(reinterpret_cast<const float4*>(p.red + s * p.src_stride + (size_t)b * K) + i);
+                    r.x += q.x;
+                    r.y += q.y;
+                    r.z += q.z;
+                    r.w += q.w;
+                }
+            }
             v.x += r.x;
             v.y += r.y;
             v.z += r.z;
@@ -486,6 +532,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                         if (b < users && 2 * col < p.rows)
                             reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)b * p.ld_out + col] =
                                 __float2bfloat16_rn(silu_f(v[b]) * up[b]);
+                }
+            } else if (EPI == EPI_P2P) {
+                // the row into every rank's window as a tagged word (one 8-byte store, remote over NVLink)
+                if (r < p.rows) {
+                    for (int d = 0; d < p.p2p_n; ++d) {
+#pragma unroll
+                        for (int b = 0; b < B; ++b)
+                            if (b < users)
+                                p.peer_data[d][(size_t)b * p.peer_ld + r] = make_uint2(__float_as_uint(v[b]), tag);
+                    }
                 }
             } else if (r < p.rows) {
 #pragma unroll
@@ -697,7 +753,8 @@ int gemv_grid(int users, int rows_pad, int K, int grid) {
 
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch) {
+                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch,
+                        const GemvExchange* ex = nullptr) {
     if (users < 1 || users > kMaxRows || w.K % 128 != 0 || w.rows_pad % kTileRows != 0 || w.rows_pad < w.rows ||
         w.rows_pad > kGemvMaxTiles * kTileRows)
         return cudaErrorInvalidValue;
@@ -720,6 +777,21 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.red = red;
     p.x_out = x_out;
     if (pro == PRO_RMSNORM_ADD && (red == nullptr || x_out == nullptr)) return cudaErrorInvalidValue;
+    const GemvExchange none;
+    const GemvExchange& e = ex ? *ex : none;
+    if (e.nsrc < 1 || e.nsrc > kMaxPeers || e.p2p_n < 0 || e.p2p_n > kMaxPeers) return cudaErrorInvalidValue;
+    if ((epi == EPI_P2P) != (e.p2p_n > 0) || (e.tagged != nullptr && pro != PRO_RMSNORM_ADD) ||
+        ((e.tagged != nullptr || e.p2p_n > 0) && e.epoch == nullptr))
+        return cudaErrorInvalidValue;
+    p.nsrc = e.nsrc;
+    p.src_stride = e.src_stride;
+    p.tagged = e.tagged;
+    p.epoch = e.epoch;
+    p.tag_mul = e.tag_mul;
+    p.tag_add = e.tag_add;
+    p.p2p_n = e.p2p_n;
+    p.peer_ld = e.peer_ld;
+    for (int i = 0; i < kMaxPeers; ++i) p.peer_data[i] = e.peer_data[i];
     p.out = out;
     p.ld_out = ld_out;
     p.err = err;
@@ -746,6 +818,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     if (pro == PRO_BF16 && epi == EPI_RESID) return launch_pe<PRO_BF16, EPI_RESID>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_F32) return launch_pe<PRO_BF16, EPI_F32>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_BF16) return launch_pe<PRO_BF16, EPI_BF16>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_BF16 && epi == EPI_P2P) return launch_pe<PRO_BF16, EPI_P2P>(p, Bt, grid, smem, st, pdl);
     return cudaErrorInvalidValue;
 }
 

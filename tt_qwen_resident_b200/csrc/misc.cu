@@ -267,7 +267,7 @@ __global__ void embed_rows_kernel(const qres_tok* tok, const float* x0, const ui
     }
 }
 
-__global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows) {
+__global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, uint32_t* epoch) {
     pdl_launch();
     pdl_wait();
     const int b = threadIdx.x;
@@ -284,7 +284,25 @@ __global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, 
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) tok->step += 1;
+    if (threadIdx.x == 0) {
+        tok->step += 1;
+        if (epoch) *epoch += 1;  // steps completed: the peer exchanges' expected counts derive from it
+    }
+}
+
+// the peer exchange of the lm_head's top-32 lists (the hubs' list exchange, mlp_hub.cpp:366-411): this rank's
+// [rows][64] list into its region of every rank's window, then one release-add per destination
+__global__ void publish_lists_kernel(const uint32_t* __restrict__ list, int words, P2PDest dst, const uint32_t* epoch) {
+    pdl_launch();
+    pdl_wait();
+    const uint32_t slot = *epoch & 1u;  // this step's half of the double buffer
+    for (int d = 0; d < dst.n; ++d)
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst.data[d][slot * dst.slot_words + i] = list[i];
+    __syncthreads();
+    if ((int)threadIdx.x < dst.n) {
+        __threadfence_system();
+        red_release_sys_add(dst.cnt[threadIdx.x] + slot * 8, 1u);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -354,10 +372,11 @@ cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16
     return cudaLaunchKernelEx(&cfg, embed_rows_kernel, tok, x0, embed, vocab, x, rows, err);
 }
 
-cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl) {
+cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl,
+                        uint32_t* epoch) {
     cudaLaunchAttribute at[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(32), 0, st, at, pdl);
-    return cudaLaunchKernelEx(&cfg, feed_kernel, tok, argmax, out, rows);
+    return cudaLaunchKernelEx(&cfg, feed_kernel, tok, argmax, out, rows, epoch);
 }
 
 }  // namespace qres
@@ -367,7 +386,8 @@ namespace qres {
 // merge nlists per-rank lists ([nlists][rows][64], keys then indices, ranks in vocab order) into one list per
 // row and its argmax (the hubs' exchange + merge, mlp_hub.cpp:366-411 / sampling.hpp merge)
 __global__ void __launch_bounds__(256) merge_lists_kernel(const uint32_t* lists, int nlists, int rows, uint32_t* out,
-                                                          int32_t* argmax) {
+                                                          int32_t* argmax, const uint32_t* wait_cnt,
+                                                          const uint32_t* epoch, uint32_t* err) {
     const int row = blockIdx.x;
     __shared__ uint16_t keys[8 * kTopK];
     __shared__ uint32_t idx[8 * kTopK];
@@ -376,12 +396,20 @@ __global__ void __launch_bounds__(256) merge_lists_kernel(const uint32_t* lists,
     __shared__ uint32_t ok_[kTopK], oi_[kTopK];
     pdl_launch();
     pdl_wait();
+    if (wait_cnt != nullptr) {
+        // the peer exchange: every rank's list of this step has arrived (one thread per rank, bounded); step s
+        // uses half s % 2 of the double buffer for the (s / 2 + 1)-th time
+        const uint32_t e = *epoch;
+        lists += (size_t)(e & 1u) * 8 * rows * 2 * kTopK;
+        if ((int)threadIdx.x < nlists) wait_count(wait_cnt + (e & 1u) * 8 + threadIdx.x, e / 2 + 1, err);
+        __syncthreads();
+    }
     const int n = nlists * kTopK;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int l = i / kTopK, j = i % kTopK;
         const uint32_t* src = lists + ((size_t)l * rows + row) * 2 * kTopK;
-        keys[i] = (uint16_t)src[j];
-        idx[i] = src[kTopK + j];
+        keys[i] = (uint16_t)__ldcg(src + j);
+        idx[i] = __ldcg(src + kTopK + j);
     }
     __syncthreads();
     block_top32(keys, idx, n, ok_, oi_, hist, scratch);
@@ -393,11 +421,20 @@ __global__ void __launch_bounds__(256) merge_lists_kernel(const uint32_t* lists,
 }
 
 cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint32_t* out, int32_t* argmax,
-                               cudaStream_t st, bool pdl) {
-    if (nlists < 1 || nlists > 8) return cudaErrorInvalidValue;
+                               cudaStream_t st, bool pdl, const uint32_t* wait_cnt, const uint32_t* epoch,
+                               uint32_t* err) {
+    if (nlists < 1 || nlists > 8 || (wait_cnt && !epoch)) return cudaErrorInvalidValue;
     cudaLaunchAttribute at[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(256), 0, st, at, pdl);
-    return cudaLaunchKernelEx(&cfg, merge_lists_kernel, lists, nlists, rows, out, argmax);
+    return cudaLaunchKernelEx(&cfg, merge_lists_kernel, lists, nlists, rows, out, argmax, wait_cnt, epoch, err);
+}
+
+cudaError_t publish_lists_launch(const uint32_t* list, int words, const P2PDest& dst, const uint32_t* epoch,
+                                 cudaStream_t st, bool pdl) {
+    if (dst.n < 1 || dst.n > 8 || !epoch) return cudaErrorInvalidValue;
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(256), 0, st, at, pdl);
+    return cudaLaunchKernelEx(&cfg, publish_lists_kernel, list, words, dst, epoch);
 }
 
 }  // namespace qres

@@ -25,7 +25,8 @@
 namespace qres {
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch);
+                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch,
+                        const GemvExchange* ex = nullptr);
 size_t gemv_workspace_bytes(int grid);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
@@ -45,12 +46,16 @@ size_t topk_workspace_bytes(int rows, int nblk);
 cudaError_t topk_launch(int rows, const uint16_t* logits, int n, int ld, int base, uint32_t* lists, int32_t* argmax,
                         void* work, int nblk, cudaStream_t st, bool pdl);
 cudaError_t merge_lists_launch(const uint32_t* lists, int nlists, int rows, uint32_t* out, int32_t* argmax,
-                               cudaStream_t st, bool pdl);
+                               cudaStream_t st, bool pdl, const uint32_t* wait_cnt = nullptr,
+                               const uint32_t* epoch = nullptr, uint32_t* err = nullptr);
+cudaError_t publish_lists_launch(const uint32_t* list, int words, const P2PDest& dst, const uint32_t* epoch,
+                                 cudaStream_t st, bool pdl);
 cudaError_t topk_static_scratch(void** out, size_t* bytes);
 size_t topk_ticket_offset(int rows, int nblk);
 cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x, int rows,
                               uint32_t* err, cudaStream_t st, bool pdl);
-cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl);
+cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl,
+                        uint32_t* epoch);
 }  // namespace qres
 
 using namespace qres;
@@ -99,6 +104,20 @@ bool load_nccl(const char* libpath, std::string* why) {
     return true;
 }
 
+// A rank's peer-exchange window (qres_p2p_*): one cudaMalloc allocation, mapped into every other rank with
+// CUDA IPC. Layout: list counters [2 slots][8 source ranks] (uint32, 256-byte header), then the row-parallel
+// partials [2 slots][8 sources][rows][5120] as tagged words {fp32 bits, tag}, then the top-32 lists
+// [2 slots][8 sources][rows][64] uint32. Row-parallel exchange j of step s uses slot j % 2 and tag
+// s * 2L + j + 1 (L layers; never 0, so the zeroed window holds no valid word); step s's lists use slot s % 2 and
+// their counters only grow (the k-th use of a slot completes at k).
+struct P2PLayout {
+    size_t lcnt = 0, data = 256, lists = 0, total = 0;
+    explicit P2PLayout(int rows) {
+        lists = data + (size_t)2 * 8 * rows * kHidden * 8;
+        total = lists + (size_t)2 * 8 * rows * 2 * QRES_TOPK * 4;
+    }
+};
+
 struct Layer {
     qres_weight w[5] = {};
     bool has[5] = {false, false, false, false, false};
@@ -139,6 +158,11 @@ struct qres_ctx {
     void* gemv_work = nullptr;
     size_t gemv_work_bytes = 0;
     ncclComm_t comm = nullptr;
+    // peer exchange (qres_p2p_alloc / qres_p2p_open): this rank's window and every rank's window as mapped here
+    uint8_t* p2p_local = nullptr;
+    uint8_t* p2p_peer[8] = {};
+    bool p2p_on = false;
+    uint32_t* epoch = nullptr;  // steps completed (workspace), advanced by the feed kernel
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
@@ -177,7 +201,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, xb, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
+    size_t err, epoch, xb, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -190,6 +214,7 @@ Carve carve(const qres_ctx* c) {
         return at;
     };
     k.err = take(256);
+    k.epoch = take(256);
     k.xb = take((size_t)R * kHidden * 4);
     k.partial = take((size_t)R * kHidden * 4);
     k.y = take((size_t)R * c->ld_y * 2);
@@ -268,6 +293,9 @@ qres_status qres_destroy(qres_ctx* ctx) {
     if (ctx->exec) cudaGraphExecDestroy(ctx->exec);
     if (ctx->graph) cudaGraphDestroy(ctx->graph);
     if (ctx->comm && g_nccl.commDestroy) g_nccl.commDestroy(ctx->comm);
+    for (int r = 0; r < ctx->nranks; ++r)
+        if (ctx->p2p_peer[r] && ctx->p2p_peer[r] != ctx->p2p_local) cudaIpcCloseMemHandle(ctx->p2p_peer[r]);
+    if (ctx->p2p_local) cudaFree(ctx->p2p_local);
     delete ctx;
     return QRES_OK;
 }
@@ -363,6 +391,7 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->ws = w;
     c->ws_bytes = bytes;
     c->err = reinterpret_cast<uint32_t*>(w + k.err);
+    c->epoch = reinterpret_cast<uint32_t*>(w + k.epoch);
     c->xb = reinterpret_cast<float*>(w + k.xb);
     c->partial = reinterpret_cast<float*>(w + k.partial);
     c->y = reinterpret_cast<uint16_t*>(w + k.y);
@@ -375,6 +404,52 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->topk_work = c->vocab_local ? (void*)(w + k.topk) : nullptr;
     c->gemv_work = w + k.gemv;
     c->gemv_work_bytes = k.gemv_bytes;
+    return QRES_OK;
+}
+
+qres_status qres_p2p_window_size(const qres_ctx* c, size_t* bytes) {
+    if (!c || !bytes) return QRES_ERR_ARG;
+    *bytes = P2PLayout(c->cfg.rows).total;
+    return QRES_OK;
+}
+
+qres_status qres_p2p_alloc(qres_ctx* c, void* handle64) {
+    if (!c || !handle64) return fail(c, QRES_ERR_ARG, "qres_p2p_alloc: null argument");
+    if (c->nranks < 2) return fail(c, QRES_ERR_ARG, "qres_p2p_alloc: one rank has no peers");
+    if (c->p2p_local) return fail(c, QRES_ERR_STATE, "qres_p2p_alloc: window already allocated");
+    const size_t bytes = P2PLayout(c->cfg.rows).total;
+    void* p = nullptr;
+    CU(c, cudaMalloc(&p, bytes));
+    c->p2p_local = static_cast<uint8_t*>(p);
+    CU(c, cudaMemset(p, 0, bytes));
+    CU(c, cudaDeviceSynchronize());
+    cudaIpcMemHandle_t h;
+    CU(c, cudaIpcGetMemHandle(&h, p));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    memcpy(handle64, &h, 64);
+    return QRES_OK;
+}
+
+qres_status qres_p2p_open(qres_ctx* c, const void* handles) {
+    if (!c || !handles) return fail(c, QRES_ERR_ARG, "qres_p2p_open: null argument");
+    if (!c->p2p_local) return fail(c, QRES_ERR_STATE, "qres_p2p_open before qres_p2p_alloc");
+    if (!c->ws) return fail(c, QRES_ERR_STATE, "qres_p2p_open before qres_bind_workspace");
+    if (c->p2p_on) return fail(c, QRES_ERR_STATE, "qres_p2p_open: already open");
+    const uint8_t* hs = static_cast<const uint8_t*>(handles);
+    for (int r = 0; r < c->nranks; ++r) {
+        if (r == c->rank) {
+            c->p2p_peer[r] = c->p2p_local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hs + (size_t)r * 64, 64);
+        void* p = nullptr;
+        CU(c, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        c->p2p_peer[r] = static_cast<uint8_t*>(p);
+    }
+    CU(c, cudaMemset(c->epoch, 0, 4));
+    CU(c, cudaDeviceSynchronize());
+    c->p2p_on = true;
     return QRES_OK;
 }
 
@@ -405,7 +480,9 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     const int R = c->cfg.rows, n = c->nranks;
     const bool tp = n > 1;
     if (!c->has_io || !c->ws) return fail(c, QRES_ERR_STATE, "decode step before bind_io / bind_workspace");
-    if (tp && !c->comm) return fail(c, QRES_ERR_STATE, "nranks > 1 needs qres_nccl_init");
+    if (tp && !c->comm && !c->p2p_on) return fail(c, QRES_ERR_STATE, "nranks > 1 needs qres_p2p_open or qres_nccl_init");
+    const bool p2p = tp && c->p2p_on;
+    const P2PLayout pl(R);
     if (c->cfg.vocab && !c->has_head) return fail(c, QRES_ERR_STATE, "lm_head not loaded");
     for (int l = 0; l < c->cfg.layers; ++l) {
         const Layer& L = c->layers[l];
@@ -433,6 +510,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     float* other = c->xb;
     STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
     bool pending = false;  // all-reduced partials waiting to be added to cur
+    int xchg = 0;          // row-parallel exchanges issued so far in this step (peer exchange: slot xchg % 2)
     auto allreduce = [&]() -> qres_status {
         ncclResult_t r = g_nccl.allReduce(c->partial, c->partial, (size_t)R * kHidden, ncclFloat32, ncclSum, c->comm, st);
         if (r != ncclSuccess) return fail(c, QRES_ERR_COMM, "ncclAllReduce: %d", (int)r);
@@ -463,6 +541,23 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                  what);
     };
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
+        if (pending && p2p) {
+            // the peer exchange xchg - 1: every rank's tagged partial, added in rank order
+            const int j = xchg - 1, slot = j & 1;
+            GemvExchange ex;
+            ex.nsrc = n;
+            ex.tagged = reinterpret_cast<const uint2*>(c->p2p_local + pl.data) + (size_t)slot * 8 * R * kHidden;
+            ex.epoch = c->epoch;
+            ex.tag_mul = 2u * (uint32_t)c->cfg.layers;
+            ex.tag_add = (uint32_t)j + 1u;
+            qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid, c->err, st, true,
+                                          reinterpret_cast<const float*>(ex.tagged), other, c->gemv_work,
+                                          c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
+                              what);
+            std::swap(cur, other);
+            pending = false;
+            return s;
+        }
         if (pending) {
             qres_status s = gemv(w, 2, cur, kHidden, epi, out, ld_out, c->partial, other, what);
             std::swap(cur, other);
@@ -473,6 +568,24 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     };
     // a row-parallel projection: residual update (one rank) or fp32 partial + all-reduce (TP)
     auto row_parallel = [&](const qres_weight& w, const uint16_t* in, const char* what) -> qres_status {
+        if (p2p) {
+            // fused exchange: the epilogue stores each finished tile into every rank's window (slot xchg % 2)
+            const int slot = xchg & 1;
+            GemvExchange ex;
+            ex.p2p_n = n;
+            ex.peer_ld = kHidden;
+            ex.epoch = c->epoch;
+            ex.tag_mul = 2u * (uint32_t)c->cfg.layers;
+            ex.tag_add = (uint32_t)xchg + 1u;
+            for (int r = 0; r < n; ++r)
+                ex.peer_data[r] = reinterpret_cast<uint2*>(c->p2p_peer[r] + pl.data) + ((size_t)slot * 8 + c->rank) * R * kHidden;
+            qres_status s = K(gemv_launch(w, R, 1, in, w.K, 4, nullptr, kHidden, grid, c->err, st, true, nullptr,
+                                          nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
+                              what);
+            ++xchg;
+            pending = true;
+            return s;
+        }
         qres_status s = gemv(w, 1, in, w.K, tp ? 3 : 2, tp ? c->partial : cur, kHidden, nullptr, nullptr, what);
         if (s || !tp) return s;
         s = allreduce();
@@ -513,6 +626,22 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, c->argmax, c->topk_work,
                              c->topk_blk, st, true),
                  "top-k");
+        } else if (p2p) {
+            STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, nullptr, c->topk_work,
+                             c->topk_blk, st, true),
+                 "top-k");
+            P2PDest dst;
+            dst.n = n;
+            dst.slot_words = (size_t)8 * R * 2 * QRES_TOPK;
+            for (int r = 0; r < n; ++r) {
+                dst.data[r] = reinterpret_cast<uint32_t*>(c->p2p_peer[r] + pl.lists) + (size_t)c->rank * R * 2 * QRES_TOPK;
+                dst.cnt[r] = reinterpret_cast<uint32_t*>(c->p2p_peer[r] + pl.lcnt) + c->rank;
+            }
+            STEP(publish_lists_launch(c->io.topk, R * 2 * QRES_TOPK, dst, c->epoch, st, true), "list exchange");
+            STEP(merge_lists_launch(reinterpret_cast<const uint32_t*>(c->p2p_local + pl.lists), n, R, c->io.topk,
+                                    c->argmax, st, true, reinterpret_cast<const uint32_t*>(c->p2p_local + pl.lcnt),
+                                    c->epoch, c->err),
+                 "merge");
         } else {
             STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, nullptr, c->topk_work,
                              c->topk_blk, st, true),
@@ -521,9 +650,9 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             if (r != ncclSuccess) return fail(c, QRES_ERR_COMM, "ncclAllGather: %d", (int)r);
             STEP(merge_lists_launch(c->gathered, n, R, c->io.topk, c->argmax, st, true), "merge");
         }
-        STEP(feed_launch(c->io.tok, c->argmax, c->io.out, R, st, true), "feed");
+        STEP(feed_launch(c->io.tok, c->argmax, c->io.out, R, st, true, c->epoch), "feed");
     } else {
-        STEP(feed_launch(c->io.tok, nullptr, nullptr, R, st, true), "feed");
+        STEP(feed_launch(c->io.tok, nullptr, nullptr, R, st, true, c->epoch), "feed");
     }
     if (cur != c->io.x) CU(c, cudaMemcpyAsync(c->io.x, cur, (size_t)R * kHidden * 4, cudaMemcpyDeviceToDevice, st));
 #undef STEP

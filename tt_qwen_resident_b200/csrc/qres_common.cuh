@@ -119,6 +119,66 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// The tensor-parallel exchange of one GEMV launch over peer memory (gemv_launch's optional argument). The
+// row-parallel projection's epilogue stores each partial as a tagged word -- {fp32 bits, tag} in one 8-byte store,
+// so a word is either wholly old or wholly new -- into its region of every rank's window; the next projection's
+// rmsnorm prologue re-reads the words until every one carries this exchange's tag and adds the ranks' partials
+// in rank order. No fence, counter or barrier sits between the two GPUs' kernels.
+struct GemvExchange {
+    int nsrc = 1;                      // prologue: partial sources to add (red, red + src_stride, ...; fp32)
+    size_t src_stride = 0;
+    const uint2* tagged = nullptr;     // prologue: tagged sources [nsrc][users][K] in this rank's window, or null
+    const uint32_t* epoch = nullptr;   // steps completed (device)
+    uint32_t tag_mul = 0, tag_add = 0; // tag of this exchange: *epoch * tag_mul + tag_add (never 0)
+    int p2p_n = 0;                     // epilogue: destinations (ranks)
+    int peer_ld = 0;                   // words per user row in a destination region
+    uint2* peer_data[8] = {};          // this rank's region in each rank's window
+};
+
+// destinations of a small per-step peer exchange, double-buffered by step parity: this rank's region in each
+// rank's window (slot 1 at + slot_words) and its counter there (slot 1 at + 8)
+struct P2PDest {
+    int n = 0;
+    size_t slot_words = 0;
+    uint32_t* data[8] = {};
+    uint32_t* cnt[8] = {};
+};
+
+// ---- peer memory (another GPU's window mapped over NVLink) -------------------------------------------------
+
+// acquire load at system scope: pairs with a peer GPU's release-add on this (local) memory
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// release add at system scope (the counter usually lives in a peer GPU's memory)
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// 16 bytes (two tagged words) read past every cache level a peer's stores could be stale in
+__device__ __forceinline__ uint4 ld_volatile128(const void* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// spin budget on a peer counter: ~2^24 polls with a short sleep (about a second), far beyond a healthy step
+constexpr uint32_t kPeerSpinLimit = 1u << 24;
+
+// wait until the counter reaches `want` (wrap-safe compare); false (error bits set) when the budget runs out
+__device__ inline bool wait_count(const uint32_t* p, uint32_t want, uint32_t* err) {
+    for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
+        if ((int32_t)(ld_acquire_sys(p) - want) >= 0) return true;
+        __nanosleep(64);
+    }
+    if (err) atomicOr(err, kErrPeer | kErrTimeout);
+    return false;
+}
+
 // global -> shared bulk copy completing on an mbarrier (sizes and addresses multiples of 16 bytes)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(

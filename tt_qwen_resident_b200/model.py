@@ -53,6 +53,7 @@ class ResidentModel:
         device="cuda",
         sm_count=0,
         nccl_id=None,
+        p2p=False,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
@@ -131,13 +132,32 @@ class ResidentModel:
         _lib.check(L.qres_workspace_size(self.ctx, ctypes.byref(sz)), self.ctx, "workspace size")
         self.ws = torch.zeros(sz.value, dtype=torch.uint8, device=dev)
         _lib.check(L.qres_bind_workspace(self.ctx, _lib.ptr(self.ws), sz.value), self.ctx, "bind workspace")
-        if nranks > 1:
-            if nccl_id is None:
-                raise ValueError("nranks > 1 needs the NCCL id (see nccl_unique_id)")
+        if nranks > 1 and nccl_id is not None:
             buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
             _lib.check(L.qres_nccl_init(self.ctx, None, buf), self.ctx, "nccl init")
+        if nranks > 1 and p2p:
+            self._open_p2p()
+        elif nranks > 1 and nccl_id is None:
+            raise ValueError("nranks > 1 needs p2p=True (fused peer exchange) or the NCCL id (see nccl_unique_id)")
         self.trace = False
         self._initial = None
+
+    def _open_p2p(self):
+        """the fused peer exchange: allocate this rank's window, all-gather the CUDA IPC handles over the default
+        torch.distributed group (every rank constructs its model collectively), map them, then a barrier so no
+        rank steps before every window is open"""
+        import torch.distributed as dist
+
+        if not dist.is_initialized():
+            raise RuntimeError("p2p=True needs an initialised torch.distributed process group (for the handle exchange)")
+        L = _lib.lib()
+        h = ctypes.create_string_buffer(64)
+        _lib.check(L.qres_p2p_alloc(self.ctx, h), self.ctx, "p2p alloc")
+        handles = [None] * self.nranks
+        dist.all_gather_object(handles, bytes(h.raw))
+        allh = ctypes.create_string_buffer(b"".join(handles), 64 * self.nranks)
+        _lib.check(L.qres_p2p_open(self.ctx, allh), self.ctx, "p2p open")
+        dist.barrier()
 
     # ------------------------------------------------------------------------------------------ binding
     def _layer_copy(self, l):
