@@ -60,8 +60,15 @@ typedef struct {
     int32_t max_pages;     /* page-table entries per user */
     int32_t num_pages;     /* pages in each attention layer's K (and V) pool */
     int32_t sm_count;      /* SMs to use; 0 = the device's (the weight-streaming kernels run 2 CTAs per SM) */
-    int32_t flags;         /* reserved, 0 */
+    int32_t flags;         /* QRES_FLAG_VERIFY, or 0 */
 } qres_config;
+
+/* qres_config.flags: the verify step (ResidentModel(verify=True), model.py:416-457): the `rows` rows (2..5) are
+ * consecutive positions p .. p+rows-1 of ONE user, run as consecutive steps inside one step (row r sees rows
+ * < r). Each GDN layer's state holds `rows` slots; row r leaves its state in slot (tok.slot + r) % rows, so
+ * continuing after accepting row k uses position p + k + 1 and slot (tok.slot + k) % rows (no rollback). The
+ * conv history and the KV cache are position-keyed and need nothing. */
+#define QRES_FLAG_VERIFY 1
 
 /* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block of the canonical matrix), in the
  * GEMV layout made by qres_tile_weight: rows in tiles of 128 (zero-padded), a tile's K in 128-wide units of
@@ -80,7 +87,7 @@ typedef struct {
 
 /* per-layer decode state (State, model.py:151-174), laid out for this rank */
 typedef struct {
-    float* gdn_state;     /* GDN layer: [rows][48/n][128][128] fp32, updated in place */
+    float* gdn_state;     /* GDN layer: [rows][48/n][128][128] fp32, updated in place (verify: [rows slots]) */
     uint16_t* conv_hist;  /* GDN layer: [rows][QRES_HIST_SLOTS][conv_ch/n] bf16 */
     uint16_t* k_pool;     /* attention layer: [num_pages][kv_heads_local][64][256] bf16 */
     uint16_t* v_pool;     /* attention layer: same */
@@ -92,7 +99,8 @@ typedef struct {
     int32_t token[QRES_MAX_ROWS]; /* token id of each row (embedding gather); < 0: take the row of x0 */
     int32_t feed;                 /* 1: the step writes its greedy token and pos + 1 back here */
     int32_t step;                 /* incremented by every step (device side) */
-    int32_t reserved[14];
+    int32_t slot;                 /* verify: the GDN state slot row 0 starts from (model.py:79 TOK_SLOT) */
+    int32_t reserved[13];
 } qres_tok;
 
 /* per-step inputs and outputs (device pointers) */

@@ -14,6 +14,7 @@ LIB_PATH = os.environ.get("QRES_LIB", os.path.join(HERE, "libqres.so"))
 QRES_MAX_ROWS = 8
 QRES_HIST_SLOTS = 8
 QRES_KV_BLOCK = 64
+QRES_FLAG_VERIFY = 1
 QRES_TOPK = 32
 W_GDN_IN, W_ATTN_IN, W_OUT, W_GATEUP, W_DOWN, W_HEAD = range(6)
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "device error", 4: "out of order", 5: "communication"}
@@ -106,8 +107,8 @@ class Io(ctypes.Structure):
     ]
 
 
-TOK_WORDS = 32  # sizeof(qres_tok) / 4: pos[8], token[8], feed, step, reserved[14]
-TOK_POS, TOK_TOKEN, TOK_FEED, TOK_STEP = 0, 8, 16, 17
+TOK_WORDS = 32  # sizeof(qres_tok) / 4: pos[8], token[8], feed, step, slot, reserved[13]
+TOK_POS, TOK_TOKEN, TOK_FEED, TOK_STEP, TOK_SLOT = 0, 8, 16, 17, 18
 
 _lib = None
 

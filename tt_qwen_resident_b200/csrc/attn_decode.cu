@@ -14,6 +14,11 @@
 // per group), and keeps an online softmax (m, l, o[256]) per head. Partials go to the workspace; the last CTA
 // of a (user, kv head) -- an atomic ticket -- combines them in chunk order (deterministic) and applies the gate.
 // The CTA whose pages hold `pos` appends k / v to the cache and uses them from shared memory for that row.
+//
+// Verify step (R consecutive positions p .. p+R-1 of one user, attn_common.hpp:39-42 KV sharing; row r sees
+// rows < r): all rows share user 0's page table; every CTA of row r computes k / v of rows 0..r itself and
+// uses them for positions p .. p+r (the cache there may be mid-append by other rows' CTAs, so it is never read
+// for those positions); each row still appends its own position.
 #include "qres_common.cuh"
 
 namespace qres {
@@ -41,6 +46,7 @@ struct AttnParams {
     float* part;              // [B][nkv][nchunks][G][2 + 256]
     int* ticket;              // [B][nkv]
     int nchunks;
+    int verify;               // 0, or R: rows are R consecutive positions of user 0
     const uint8_t* pf;        // the next projection's weights: prefetched into L2 while this kernel runs
     size_t pf_bytes;
     uint32_t* err;
@@ -84,8 +90,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + 4 * (size_t)kPageBytes);
 
     __shared__ float qf[kMaxGroup][kHD];
-    __shared__ float knew[kHD];
-    __shared__ float vnew[kHD];
+    __shared__ float knew[kMaxRows][kHD];  // k / v of the positions this step writes (row order)
+    __shared__ float vnew[kMaxRows][kHD];
     __shared__ float sc[kMaxGroup][kKvBlock];
     __shared__ float red[8];
     __shared__ float mrow[kMaxGroup], corr[kMaxGroup], lrow[kMaxGroup];
@@ -109,7 +115,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     pdl_wait();
 
     const int pos = p.pos[b];
-    if (pos < 0 || pos >= p.max_pos || pos / kKvBlock >= p.max_pages) {
+    const int p0 = p.verify ? p.pos[0] : pos;  // first position this step writes (new k / v from p0 on)
+    if (pos < 0 || pos >= p.max_pos || pos / kKvBlock >= p.max_pages || (p.verify && pos != p0 + b)) {
         if (tid == 0) atomicOr(p.err, kErrBounds);
         return;
     }
@@ -117,7 +124,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const int npg = (L + kKvBlock - 1) / kKvBlock;
     const int ppc = (npg + p.nchunks - 1) / p.nchunks;
     const int pg0 = c * ppc, pg1 = min(pg0 + ppc, npg);
-    const int* pt = p.page_table + (size_t)b * p.max_pages;
+    const int* pt = p.page_table + (size_t)(p.verify ? 0 : b) * p.max_pages;
     const uint16_t* y = p.y + (size_t)b * p.ld_y;
     const float* cs = p.cos_tab + (size_t)pos * (kRot / 2);
     const float* sn = p.sin_tab + (size_t)pos * (kRot / 2);
@@ -148,18 +155,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     // q of the group's heads (fp32)
     for (int j = 0; j < G; ++j)
         rms_rope_head(y + (size_t)(g * G + j) * kHD, p.wq, cs, sn, qf[j], red, false);
+    // k / v of the new positions p0 .. pos whose pages this CTA covers (row j's from its own y row)
+    const int kbase = 2 * p.h * kHD;
+    const int pg_lo = pg0 * kKvBlock, pg_hi = pg1 * kKvBlock;  // positions of this CTA's pages
+    for (int t = max(p0, pg_lo); t <= pos && t < pg_hi; ++t) {
+        const int j = t - p0;
+        const uint16_t* yj = p.y + (size_t)(p.verify ? j : b) * p.ld_y;
+        rms_rope_head(yj + kbase + (size_t)g * kHD, p.wk, p.cos_tab + (size_t)t * (kRot / 2),
+                      p.sin_tab + (size_t)t * (kRot / 2), knew[j], red, true);
+        vnew[j][tid] = __uint_as_float((uint32_t)yj[kbase + p.nkv * kHD + g * kHD + tid] << 16);
+    }
     const bool has_pos = pg0 <= pos / kKvBlock && pos / kKvBlock < pg1;
     if (has_pos) {
-        const int kbase = 2 * p.h * kHD;
-        rms_rope_head(y + kbase + (size_t)g * kHD, p.wk, cs, sn, knew, red, true);
-        vnew[tid] = __uint_as_float((uint32_t)y[kbase + p.nkv * kHD + g * kHD + tid] << 16);
         __syncthreads();
-        // append the row to the cache
+        // append this row to the cache
         const int pg = pt[pos / kKvBlock];
         const size_t off = ((size_t)pg * p.nkv + g) * head_stride + (size_t)(pos % kKvBlock) * kHD + tid;
-        p.kp[off] = __bfloat16_as_ushort(__float2bfloat16_rn(knew[tid]));
-        p.vp[off] = __bfloat16_as_ushort(__float2bfloat16_rn(vnew[tid]));
+        p.kp[off] = __bfloat16_as_ushort(__float2bfloat16_rn(knew[pos - p0][tid]));
+        p.vp[off] = __bfloat16_as_ushort(__float2bfloat16_rn(vnew[pos - p0][tid]));
     }
+    __syncthreads();
 
     float qreg[kMaxGroup][8];
 #pragma unroll
@@ -185,12 +200,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         for (int r = warp; r < kKvBlock; r += 8) {
             const int t = t0 + r;
             float dot[kMaxGroup];
-            if (t == pos) {
+            if (t >= p0 && t <= pos) {
+                const float* kn = knew[t - p0];
 #pragma unroll
                 for (int j = 0; j < kMaxGroup; ++j) {
                     float a = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) a = fmaf(qreg[j][e], knew[lane * 8 + e], a);
+                    for (int e = 0; e < 8; ++e) a = fmaf(qreg[j][e], kn[lane * 8 + e], a);
                     dot[j] = a;
                 }
             } else {
@@ -241,7 +257,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
             for (int r = 0; r < kKvBlock; ++r) {
                 const int t = t0 + r;
                 if (t > pos) break;
-                const float vv = t == pos ? vnew[d] : __uint_as_float((uint32_t)Vs[r * kHD + d] << 16);
+                const float vv = t >= p0 ? vnew[t - p0][d] : __uint_as_float((uint32_t)Vs[r * kHD + d] << 16);
 #pragma unroll
                 for (int j = 0; j < kMaxGroup; ++j) acc[j] = fmaf(sc[j][r], vv, acc[j]);
             }
@@ -334,8 +350,8 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
                         void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
-                        const void* pf, size_t pf_bytes) {
-    if (nranks < 1 || 24 % nranks || rows < 1 || rows > kMaxRows) return cudaErrorInvalidValue;
+                        const void* pf, size_t pf_bytes, int verify) {
+    if (nranks < 1 || 24 % nranks || rows < 1 || rows > kMaxRows || (verify && verify != rows)) return cudaErrorInvalidValue;
     if (work_bytes < attn_workspace_bytes(nranks, rows, nchunks)) return cudaErrorInvalidValue;
     AttnParams p;
     p.h = 24 / nranks;
@@ -361,6 +377,7 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
     p.part = static_cast<float*>(work);
     p.ticket = reinterpret_cast<int*>(static_cast<uint8_t*>(work) + part + 256);
     p.nchunks = nchunks;
+    p.verify = verify;
     p.pf = static_cast<const uint8_t*>(pf);
     p.pf_bytes = pf_bytes;
     p.err = err;

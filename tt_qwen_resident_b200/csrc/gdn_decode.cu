@@ -18,6 +18,14 @@
 // Conv history: a ring of QRES_HIST_SLOTS slots per user, position q's input in slot q % 8. A step at p reads
 // the slots of p-3..p-1 and writes slot p (never a slot it reads), so the CTAs sharing a key head all read the q
 // / k history while one of them writes it.
+//
+// Verify step (ResidentModel(verify=True), the reference's verify rows model.py:416-457, gdn_head_reader.cpp
+// :367-370 / :523-537): the rows are R <= 5 consecutive positions p .. p+R-1 of one user, run as R consecutive
+// steps inside one launch: the cluster keeps the head's state in registers from row to row, row r's conv window
+// takes the inputs at p .. p+r from the step's own rows (and p+r-3 .. p-1 from the ring, which this step never
+// writes since R + 3 <= 8), and row r's state goes to slot (slot0 + r) % R of the user's R state slots (slot0:
+// the token state's slot, holding the state row 0 starts from). Continuing after accepting row k means slot0 +
+// k and position p + k + 1: no rollback is needed.
 #include <cooperative_groups.h>
 
 #include "qres_common.cuh"
@@ -39,7 +47,9 @@ struct GdnParams {
     const float* dt;         // [nv]
     const float* neg_a;      // [nv]
     const float* norm_w;     // [128]
-    float* state;            // [B][nv][128][128]
+    float* state;            // [B][nv][128][128]; verify: [R slots][nv][128][128] of the one user
+    int verify;              // 0, or R: the rows are R consecutive positions of one user
+    const int32_t* slot0;    // verify: the state slot row 0 starts from (device, the token state)
     uint16_t* hist;          // [B][8][conv]
     uint16_t* o;             // [B][nv * 128] bf16
     uint16_t* mixer_copy;    // optional second output
@@ -70,172 +80,190 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
     pdl_launch();
     // thread layout over the CTA's 128 x 32 slice: column quad cq (4 columns), rows 8rp .. 8rp+7
     const int cq = tid & 7, rp = tid >> 3;
-    float* S = p.state + (((size_t)b * p.nv + hh) * kDK) * kDV + c0;
+    const int R = p.verify;  // verify: rows of the one user, run in order in this cluster
+    const int nrows = R ? R : 1;
+    const size_t slot_stride = (size_t)p.nv * kDK * kDV;
     // Before griddepcontrol.wait only immutable data may be read (an earlier kernel of the stream may still be
     // running); an L2 prefetch of the slice is safe (L2 is the point of coherence) and starts its 16 KB early.
-    if (tid < kDK) bulk_prefetch_l2(S + (size_t)tid * kDV, kGdnCols * 4);
+    if (!R && tid < kDK) {
+        const float* S0 = p.state + (((size_t)b * p.nv + hh) * kDK) * kDV + c0;
+        bulk_prefetch_l2(S0 + (size_t)tid * kDV, kGdnCols * 4);
+    }
     // the following projection's weights (immutable) stream into L2 meanwhile: this kernel is latency-bound
     if (p.pf && tid == 0) {
         const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
     }
     pdl_wait();
-    const int pos = p.pos[b];
-    const bool bad = pos < 0;  // uniform over the cluster (same user)
+    const int s0slot = R ? *p.slot0 : 0;
+    const int p0 = p.pos[R ? 0 : b];  // verify: row 0's position
+    // the whole launch agrees on validity (uniform over the cluster): positions, and verify's rows / slot
+    bool bad = p0 < 0 || (R && (s0slot < 0 || s0slot >= R));
+    for (int r = 1; R && r < R; ++r) bad = bad || p.pos[r] != p0 + r;
     float4 s[8];
     if (!bad) {
+        const float* Sin = p.state + (R ? (size_t)s0slot * slot_stride : (size_t)b * slot_stride) +
+                           (size_t)hh * kDK * kDV + c0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) s[i] = reinterpret_cast<const float4*>(S + (size_t)(rp * 8 + i) * kDV)[cq];
-        const uint16_t* y = p.y + (size_t)b * p.ld_y;
-        uint16_t* hist = p.hist + (size_t)b * QRES_HIST_SLOTS * conv;
-        const int s0 = (pos + QRES_HIST_SLOTS - 3) % QRES_HIST_SLOTS;
-        const int s1 = (pos + QRES_HIST_SLOTS - 2) % QRES_HIST_SLOTS;
-        const int s2 = (pos + QRES_HIST_SLOTS - 1) % QRES_HIST_SLOTS;
-        const int swr = pos % QRES_HIST_SLOTS;
-        // ---- conv1d + SiLU: q, k of the key head (256 channels) and this CTA's 32 v channels
-        for (int i = tid; i < 2 * kDK + kGdnCols; i += kGdnThreads) {
-            int ch, which;
-            if (i < kDK) {
-                ch = kh * kDK + i;
-                which = 0;
-            } else if (i < 2 * kDK) {
-                ch = gq + kh * kDK + (i - kDK);
-                which = 1;
-            } else {
-                ch = 2 * gq + hh * kDV + c0 + (i - 2 * kDK);
-                which = 2;
-            }
-            const uint16_t yin = y[ch];
-            const float w0 = __uint_as_float((uint32_t)hist[s0 * conv + ch] << 16);
-            const float w1 = __uint_as_float((uint32_t)hist[s1 * conv + ch] << 16);
-            const float w2 = __uint_as_float((uint32_t)hist[s2 * conv + ch] << 16);
-            const float w3 = __uint_as_float((uint32_t)yin << 16);
-            const uint2 tp = *reinterpret_cast<const uint2*>(p.taps + (size_t)ch * 4);
-            const float t0 = bf16lo(tp.x), t1 = bf16hi(tp.x), t2 = bf16lo(tp.y), t3 = bf16hi(tp.y);
-            float acc = mul_rn(w0, t0);
-            acc = add_rn(acc, mul_rn(w1, t1));
-            acc = add_rn(acc, mul_rn(w2, t2));
-            acc = add_rn(acc, mul_rn(w3, t3));
-            const float c = bf16_round(silu_f(acc));
-            if (which == 0) qk[0][i] = c;
-            else if (which == 1) qk[1][i - kDK] = c;
-            else vv[i - 2 * kDK] = c;
-            // one writer per history element: the key head's first value head, quarter 0, for q / k; every
-            // quarter for its v columns
-            if (which == 2 || (hh % group == 0 && qtr == 0)) hist[swr * conv + ch] = yin;
-        }
+        for (int i = 0; i < 8; ++i) s[i] = reinterpret_cast<const float4*>(Sin + (size_t)(rp * 8 + i) * kDV)[cq];
     }
-    __syncthreads();
-    if (!bad) {
-        // ---- l2 norms of q (warps 0, 1) and k (warps 2, 3)
-        {
+    uint16_t* hist = p.hist + (size_t)(R ? 0 : b) * QRES_HIST_SLOTS * conv;
+    for (int row = 0; row < nrows; ++row) {
+        const int bb = R ? row : b;  // the row's index in y / o
+        const int pos = p0 + (R ? row : 0);
+        const uint16_t* y = p.y + (size_t)bb * p.ld_y;
+        float* S = p.state + (R ? (size_t)((s0slot + row) % R) * slot_stride : (size_t)b * slot_stride) +
+                   (size_t)hh * kDK * kDV + c0;
+        if (!bad) {
+            const int swr = pos % QRES_HIST_SLOTS;
+            // ---- conv1d + SiLU: q, k of the key head (256 channels) and this CTA's 32 v channels
+            for (int i = tid; i < 2 * kDK + kGdnCols; i += kGdnThreads) {
+                int ch, which;
+                if (i < kDK) {
+                    ch = kh * kDK + i;
+                    which = 0;
+                } else if (i < 2 * kDK) {
+                    ch = gq + kh * kDK + (i - kDK);
+                    which = 1;
+                } else {
+                    ch = 2 * gq + hh * kDV + c0 + (i - 2 * kDK);
+                    which = 2;
+                }
+                const uint16_t yin = y[ch];
+                // window positions pos-3 .. pos: from the ring below p0, from this step's rows from p0 on
+                float w[4];
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const int q = pos - 3 + j;
+                    const uint16_t hv = q >= p0 && R ? p.y[(size_t)(q - p0) * p.ld_y + ch]
+                                                     : hist[(size_t)((q + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv + ch];
+                    w[j] = __uint_as_float((uint32_t)hv << 16);
+                }
+                w[3] = __uint_as_float((uint32_t)yin << 16);
+                const uint2 tp = *reinterpret_cast<const uint2*>(p.taps + (size_t)ch * 4);
+                const float t0 = bf16lo(tp.x), t1 = bf16hi(tp.x), t2 = bf16lo(tp.y), t3 = bf16hi(tp.y);
+                float acc = mul_rn(w[0], t0);
+                acc = add_rn(acc, mul_rn(w[1], t1));
+                acc = add_rn(acc, mul_rn(w[2], t2));
+                acc = add_rn(acc, mul_rn(w[3], t3));
+                const float c = bf16_round(silu_f(acc));
+                if (which == 0) qk[0][i] = c;
+                else if (which == 1) qk[1][i - kDK] = c;
+                else vv[i - 2 * kDK] = c;
+                // one writer per history element: the key head's first value head, quarter 0, for q / k; every
+                // quarter for its v columns
+                if (which == 2 || (hh % group == 0 && qtr == 0)) hist[swr * conv + ch] = yin;
+            }
+        }
+        __syncthreads();
+        if (!bad) {
+            // ---- l2 norms of q (warps 0, 1) and k (warps 2, 3)
             const int which = warp >> 1;
             const float v0 = qk[which][(warp & 1) * 64 + lane], v1 = qk[which][(warp & 1) * 64 + 32 + lane];
             const float ss = warp_sum(v0 * v0 + v1 * v1);
             if (lane == 0) sc[warp] = ss;
         }
-    }
-    __syncthreads();
-    float decay = 0.f;
-    if (!bad) {
-        for (int i = tid; i < 2 * kDK; i += kGdnThreads) {
-            const int which = i >> 7, e = i & 127;
-            const float ssum = sc[2 * which] + sc[2 * which + 1];
-            const float r = rsqrt_ieee(ssum + 1e-6f);
-            const float v = mul_rn(qk[which][e], r);
-            if (which == 0) qs[e] = mul_rn(v, 0.08838834764831845f);
-            else ks[e] = v;
+        __syncthreads();
+        float decay = 0.f;
+        if (!bad) {
+            for (int i = tid; i < 2 * kDK; i += kGdnThreads) {
+                const int which = i >> 7, e = i & 127;
+                const float ssum = sc[2 * which] + sc[2 * which + 1];
+                const float r = rsqrt_ieee(ssum + 1e-6f);
+                const float v = mul_rn(qk[which][e], r);
+                if (which == 0) qs[e] = mul_rn(v, 0.08838834764831845f);
+                else ks[e] = v;
+            }
+            const int a_off = 2 * gq + 2 * gv;
+            const float av = __uint_as_float((uint32_t)y[a_off + hh] << 16);
+            decay = expf(mul_rn(p.neg_a[hh], softplus_f(add_rn(av, p.dt[hh]))));
         }
-        const uint16_t* y = p.y + (size_t)b * p.ld_y;
-        const int a_off = 2 * gq + 2 * gv;
-        const float av = __uint_as_float((uint32_t)y[a_off + hh] << 16);
-        decay = expf(mul_rn(p.neg_a[hh], softplus_f(add_rn(av, p.dt[hh]))));
-    }
-    __syncthreads();
-    float part[4] = {0.f, 0.f, 0.f, 0.f};
-    if (!bad) {
-        // ---- kS = (decay * kn) @ S over this CTA's columns
+        __syncthreads();
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!bad) {
+            // ---- kS = (decay * kn) @ S over this CTA's columns
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float dk = mul_rn(decay, ks[rp * 8 + i]);
-            part[0] = fmaf(dk, s[i].x, part[0]);
-            part[1] = fmaf(dk, s[i].y, part[1]);
-            part[2] = fmaf(dk, s[i].z, part[2]);
-            part[3] = fmaf(dk, s[i].w, part[3]);
+            for (int i = 0; i < 8; ++i) {
+                const float dk = mul_rn(decay, ks[rp * 8 + i]);
+                part[0] = fmaf(dk, s[i].x, part[0]);
+                part[1] = fmaf(dk, s[i].y, part[1]);
+                part[2] = fmaf(dk, s[i].z, part[2]);
+                part[3] = fmaf(dk, s[i].w, part[3]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[rp][4 * cq + j] = part[j];
         }
+        __syncthreads();
+        if (!bad && tid < kGdnCols) {
+            const float bv = __uint_as_float((uint32_t)y[2 * gq + 2 * gv + p.nv + hh] << 16);
+            const float beta = sigmoid_f(bv);
+            float t = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) red[rp][4 * cq + j] = part[j];
-    }
-    __syncthreads();
-    if (!bad && tid < kGdnCols) {
-        const uint16_t* y = p.y + (size_t)b * p.ld_y;
-        const float bv = __uint_as_float((uint32_t)y[2 * gq + 2 * gv + p.nv + hh] << 16);
-        const float beta = sigmoid_f(bv);
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < 16; ++w) t += red[w][tid];
-        dl[tid] = mul_rn(beta, vv[tid] - t);
-    }
-    __syncthreads();
-    if (!bad) {
-        // ---- S <- decay * S + kn (x) delta, o = qn @ S
-        const float d0 = dl[4 * cq], d1 = dl[4 * cq + 1], d2 = dl[4 * cq + 2], d3 = dl[4 * cq + 3];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) part[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float kn = ks[rp * 8 + i], qn = qs[rp * 8 + i];
-            float4 v = s[i];
-            v.x = add_rn(mul_rn(decay, v.x), mul_rn(kn, d0));
-            v.y = add_rn(mul_rn(decay, v.y), mul_rn(kn, d1));
-            v.z = add_rn(mul_rn(decay, v.z), mul_rn(kn, d2));
-            v.w = add_rn(mul_rn(decay, v.w), mul_rn(kn, d3));
-            reinterpret_cast<float4*>(S + (size_t)(rp * 8 + i) * kDV)[cq] = v;
-            part[0] = fmaf(qn, v.x, part[0]);
-            part[1] = fmaf(qn, v.y, part[1]);
-            part[2] = fmaf(qn, v.z, part[2]);
-            part[3] = fmaf(qn, v.w, part[3]);
+            for (int w = 0; w < 16; ++w) t += red[w][tid];
+            dl[tid] = mul_rn(beta, vv[tid] - t);
         }
-    }
-    __syncthreads();  // red reused
-    if (!bad) {
+        __syncthreads();
+        if (!bad) {
+            // ---- S <- decay * S + kn (x) delta, o = qn @ S
+            const float d0 = dl[4 * cq], d1 = dl[4 * cq + 1], d2 = dl[4 * cq + 2], d3 = dl[4 * cq + 3];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) red[rp][4 * cq + j] = part[j];
-    }
-    __syncthreads();
-    float ov = 0.f;
-    if (!bad && warp == 0) {
+            for (int j = 0; j < 4; ++j) part[j] = 0.f;
 #pragma unroll
-        for (int w = 0; w < 16; ++w) ov += red[w][lane];
-        const float sq = warp_sum(ov * ov);
-        if (lane == 0) osq = sq;
-    }
-    // ---- gated RMSNorm: the sum of o^2 over the head's 4 CTAs, read through distributed shared memory
-    cluster.sync();
-    if (!bad && warp == 0) {
-        float tot = 0.f;
+            for (int i = 0; i < 8; ++i) {
+                const float kn = ks[rp * 8 + i], qn = qs[rp * 8 + i];
+                float4 v = s[i];
+                v.x = add_rn(mul_rn(decay, v.x), mul_rn(kn, d0));
+                v.y = add_rn(mul_rn(decay, v.y), mul_rn(kn, d1));
+                v.z = add_rn(mul_rn(decay, v.z), mul_rn(kn, d2));
+                v.w = add_rn(mul_rn(decay, v.w), mul_rn(kn, d3));
+                s[i] = v;  // the next row (verify) continues from it
+                reinterpret_cast<float4*>(S + (size_t)(rp * 8 + i) * kDV)[cq] = v;
+                part[0] = fmaf(qn, v.x, part[0]);
+                part[1] = fmaf(qn, v.y, part[1]);
+                part[2] = fmaf(qn, v.z, part[2]);
+                part[3] = fmaf(qn, v.w, part[3]);
+            }
+        }
+        __syncthreads();  // red reused
+        if (!bad) {
 #pragma unroll
-        for (int r = 0; r < kGdnSplit; ++r) tot += *cluster.map_shared_rank(&osq, r);
-        const float mean = tot / (float)kDV;
-        const float rr = rsqrt_ieee(mean + kEps);
-        const int col = c0 + lane;
-        const float on = mul_rn(mul_rn(ov, rr), p.norm_w[col]);
-        const uint16_t* y = p.y + (size_t)b * p.ld_y;
-        const float z = __uint_as_float((uint32_t)y[2 * gq + gv + hh * kDV + col] << 16);
-        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(on, silu_f(z)));
-        const size_t idx = (size_t)b * gv + hh * kDV + col;
-        reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
-        if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
+            for (int j = 0; j < 4; ++j) red[rp][4 * cq + j] = part[j];
+        }
+        __syncthreads();
+        float ov = 0.f;
+        if (!bad && warp == 0) {
+#pragma unroll
+            for (int w = 0; w < 16; ++w) ov += red[w][lane];
+            const float sq = warp_sum(ov * ov);
+            if (lane == 0) osq = sq;
+        }
+        // ---- gated RMSNorm: the sum of o^2 over the head's 4 CTAs, read through distributed shared memory
+        cluster.sync();
+        if (!bad && warp == 0) {
+            float tot = 0.f;
+#pragma unroll
+            for (int r = 0; r < kGdnSplit; ++r) tot += *cluster.map_shared_rank(&osq, r);
+            const float mean = tot / (float)kDV;
+            const float rr = rsqrt_ieee(mean + kEps);
+            const int col = c0 + lane;
+            const float on = mul_rn(mul_rn(ov, rr), p.norm_w[col]);
+            const float z = __uint_as_float((uint32_t)y[2 * gq + gv + hh * kDV + col] << 16);
+            const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(on, silu_f(z)));
+            const size_t idx = (size_t)bb * gv + hh * kDV + col;
+            reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
+            if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
+        }
+        cluster.sync();  // osq is rewritten by the next row; no CTA leaves while a peer may still read it
     }
     if (bad && tid == 0 && qtr == 0) atomicOr(p.err, kErrBounds);
-    cluster.sync();  // no CTA leaves while a peer may still read its shared memory
 }
 
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
-                       const void* pf, size_t pf_bytes) {
+                       const void* pf, size_t pf_bytes, int verify, const int32_t* slot0) {
     if (nranks < 1 || 16 % nranks || rows < 1 || rows > kMaxRows) return cudaErrorInvalidValue;
+    if (verify && (verify != rows || rows + 3 > QRES_HIST_SLOTS || slot0 == nullptr)) return cudaErrorInvalidValue;
     GdnParams p;
     p.nk = 16 / nranks;
     p.nv = 48 / nranks;
@@ -253,8 +281,10 @@ cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const 
     p.pf = static_cast<const uint8_t*>(pf);
     p.pf_bytes = pf_bytes;
     p.err = err;
+    p.verify = verify;
+    p.slot0 = slot0;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.nv, rows, kGdnSplit);
+    cfg.gridDim = dim3(p.nv, verify ? 1 : rows, kGdnSplit);
     cfg.blockDim = dim3(kGdnThreads);
     cfg.stream = st;
     cudaLaunchAttribute at[1];

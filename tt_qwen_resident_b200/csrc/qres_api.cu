@@ -31,14 +31,14 @@ size_t gemv_workspace_bytes(int grid);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
-                       const void* pf, size_t pf_bytes);
+                       const void* pf, size_t pf_bytes, int verify = 0, const int32_t* slot0 = nullptr);
 size_t attn_workspace_bytes(int nranks, int rows, int nchunks);
 int attn_default_chunks(int nranks, int rows, int sm_count, int max_pages);
 cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const int32_t* page_table,
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
                         void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
-                        const void* pf, size_t pf_bytes);
+                        const void* pf, size_t pf_bytes, int verify = 0);
 cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st);
 cudaError_t quantize_fp8_launch(const float* w, int N, int K, uint8_t* q, float* scales, cudaStream_t st);
 int topk_default_blocks(int n);
@@ -263,6 +263,10 @@ qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qr
     if (cfg->rows < 1 || cfg->rows > QRES_MAX_ROWS || cfg->layers < 1)
         return fail(nullptr, QRES_ERR_ARG, "qres_create: rows %d, layers %d", cfg->rows, cfg->layers);
     if (cfg->vocab % nranks) return fail(nullptr, QRES_ERR_ARG, "qres_create: vocab %d not divisible by %d", cfg->vocab, nranks);
+    if (cfg->flags & ~QRES_FLAG_VERIFY) return fail(nullptr, QRES_ERR_ARG, "qres_create: unknown flags %#x", cfg->flags);
+    if ((cfg->flags & QRES_FLAG_VERIFY) && (cfg->rows < 2 || cfg->rows + 3 > QRES_HIST_SLOTS))
+        return fail(nullptr, QRES_ERR_ARG, "qres_create: a verify step has 2..%d rows, not %d", QRES_HIST_SLOTS - 3,
+                    cfg->rows);
     qres_ctx* c = new qres_ctx();
     c->cfg = *cfg;
     c->rank = rank;
@@ -482,6 +486,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     if (!c->has_io || !c->ws) return fail(c, QRES_ERR_STATE, "decode step before bind_io / bind_workspace");
     if (tp && !c->comm && !c->p2p_on) return fail(c, QRES_ERR_STATE, "nranks > 1 needs qres_p2p_open or qres_nccl_init");
     const bool p2p = tp && c->p2p_on;
+    const int verify = (c->cfg.flags & QRES_FLAG_VERIFY) ? R : 0;
     const P2PLayout pl(R);
     if (c->cfg.vocab && !c->has_head) return fail(c, QRES_ERR_STATE, "lm_head not loaded");
     for (int l = 0; l < c->cfg.layers; ++l) {
@@ -604,11 +609,11 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (at) {
             STEP(attn_launch(n, R, c->y, c->ld_y, pos, c->io.page_table, c->cfg.max_pages, c->cfg.num_pages, L.wq, L.wk,
                              c->cos_tab, c->sin_tab, c->max_pos, L.st.k_pool, L.st.v_pool, c->o, mcopy, c->attn_work,
-                             c->attn_work_bytes, c->attn_chunks, c->err, st, true, pf, pf_bytes),
+                             c->attn_work_bytes, c->attn_chunks, c->err, st, true, pf, pf_bytes, verify),
                  "attention");
         } else {
             STEP(gdn_launch(n, R, c->y, c->ld_y, pos, L.taps, L.dt, L.neg_a, L.norm_w, L.st.gdn_state, L.st.conv_hist,
-                            c->o, mcopy, c->err, st, true, pf, pf_bytes),
+                            c->o, mcopy, c->err, st, true, pf, pf_bytes, verify, &c->io.tok->slot),
                  "gdn");
         }
         s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");

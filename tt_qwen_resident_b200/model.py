@@ -54,6 +54,7 @@ class ResidentModel:
         sm_count=0,
         nccl_id=None,
         p2p=False,
+        verify=False,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
@@ -62,6 +63,12 @@ class ResidentModel:
         rows (device-fed decode). page_table: [batch, max_pages] int32 (default: user b's pages contiguous)."""
         self.device = torch.device(device)
         self.layers, self.interval, self.batch = layers, interval, batch
+        # verify (model.py:416-457): the batch rows are consecutive positions of ONE user (row r sees rows < r);
+        # each GDN state holds `batch` slots (row r leaves its state in slot (slot + r) % batch)
+        self.verify = bool(verify)
+        if self.verify:
+            assert 2 <= batch <= _lib.QRES_HIST_SLOTS - 3, "a verify step has 2..5 rows"
+            assert state_copies is None, "verify: one GDN state / KV cache per layer"
         self.users = batch
         self.rank, self.nranks = rank, nranks
         self.lm_head = lm_head and w.get("head") is not None
@@ -75,7 +82,8 @@ class ResidentModel:
         gc, ac = state_copies or (self.n_gdn, self.n_attn)
         self.state_copies = (max(gc, 1) if self.n_gdn else 0, max(ac, 1) if self.n_attn else 0)
         L = _lib.lib()
-        cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count, 0)
+        cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count,
+                          _lib.QRES_FLAG_VERIFY if self.verify else 0)
         h = ctypes.c_void_p()
         _lib.check(L.qres_create(ctypes.byref(cfg), rank, nranks, ctypes.byref(h)), None, "qres_create")
         self.ctx = h
@@ -228,10 +236,16 @@ class ResidentModel:
         return self.batch * (gdn + kv)
 
     # ------------------------------------------------------------------------------------------ token state
-    def token_state(self, x0=None, pos=0, tokens=None, feed=False):
+    def token_state(self, x0=None, pos=0, tokens=None, feed=False, slot=0):
         """host token state (model.py:1314-1351): x0 [HIDDEN] or [batch, HIDDEN] rows (bf16 values) or token ids
-        (gathered from the embedding on device), at position(s) pos. Returns (words int32 [32], x0 or None)."""
+        (gathered from the embedding on device), at position(s) pos. Verify: pos is row 0's position (rows at
+        pos .. pos + batch - 1) and slot the GDN state slot row 0 starts from; after a step at (p, s), continuing
+        from row k is (p + k + 1, (s + k) % batch). Returns (words int32 [32], x0 or None)."""
         B = self.batch
+        if self.verify:
+            p0 = pos[0] if isinstance(pos, (list, tuple)) else pos
+            pos = [p0 + r for r in range(B)]
+            assert 0 <= slot < B, slot
         pos = [pos] * B if not isinstance(pos, (list, tuple)) else list(pos)
         assert len(pos) == B and all(0 <= p < self.max_pos for p in pos), pos
         words = torch.zeros(_lib.TOK_WORDS, dtype=torch.int32)
@@ -245,6 +259,7 @@ class ResidentModel:
             words[_lib.TOK_TOKEN : _lib.TOK_TOKEN + B] = -1
             xr = x0.reshape(B, HIDDEN).float()
         words[_lib.TOK_FEED] = int(feed)
+        words[_lib.TOK_SLOT] = int(slot)
         return words, xr
 
     def write_token_state(self, tok):
@@ -318,18 +333,21 @@ class ResidentModel:
         return int(o[0]), int(o[1])
 
     # ------------------------------------------------------------------------------------------ state
-    def load_state(self, st, user=0):
+    def load_state(self, st, user=0, slot=0):
         """write a decode state (attributes pos, gdn [copies][48,128,128], hist [copies][3, 10240] for positions
-        pos-3..pos-1, K / V [copies][4, max_pos, 256]) as user `user`'s (model.py:1447-1470)"""
+        pos-3..pos-1, K / V [copies][4, max_pos, 256]) as user `user`'s (model.py:1447-1470); verify: the one
+        user's, its GDN states into state slot `slot`"""
         d, dev = self.d, self.device
         ch = d.conv_channels()
+        if self.verify:
+            assert user == 0
         for c in range(self.state_copies[0]):
             if c < len(st.gdn):
-                self.gdn_state[c][user].copy_(st.gdn[c][d.r * d.nv : (d.r + 1) * d.nv].to(dev))
+                self.gdn_state[c][slot if self.verify else user].copy_(st.gdn[c][d.r * d.nv : (d.r + 1) * d.nv].to(dev))
                 h = st.hist[c][:, ch].to(dev).bfloat16()
                 for age in range(3):
-                    slot = (st.pos - 3 + age) % _lib.QRES_HIST_SLOTS
-                    self.conv_hist[c][user, slot] = h[age]
+                    ring = (st.pos - 3 + age) % _lib.QRES_HIST_SLOTS
+                    self.conv_hist[c][user, ring] = h[age]
         for c in range(self.state_copies[1]):
             if c < len(st.K):
                 P = min(st.pos, st.K[c].shape[1])
@@ -344,6 +362,7 @@ class ResidentModel:
         torch.cuda.synchronize(dev)
 
     def dump_gdn_state(self, copy=0, user=0):
+        """GDN state of layer copy `copy`: user `user`'s, or (verify) state slot `user`"""
         return self.gdn_state[copy][user].cpu()
 
     def kv_rows(self, copy, positions, user=0, which="K"):
