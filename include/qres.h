@@ -43,7 +43,11 @@ typedef enum {
     QRES_W_OUT = 2,     /* out-projection, 5120 rows, K = 6144 / nranks (row-parallel) */
     QRES_W_GATEUP = 3,  /* gate|up rows interleaved in pairs (g0 g1 u0 u1 ...), K = 5120 */
     QRES_W_DOWN = 4,    /* down-projection, 5120 rows, K = 17408 / nranks (row-parallel) */
-    QRES_W_HEAD = 5     /* lm_head rows of the rank's vocab slice, K = 5120 */
+    QRES_W_HEAD = 5,    /* lm_head rows of the rank's vocab slice, K = 5120 */
+    QRES_W_FC = 6       /* MTP draft layer fc (mtp.py:54-60): 5120 rows, K = 10240 = [embedding | hidden] columns
+                         * with the pre-fc norm weights (1 + w) folded in; layer ignored; one rank. A context
+                         * with an fc forms layer 0's residual as fc([rmsnorm(e) | rmsnorm(h)]) (e = the token's
+                         * embedding row, h = io.h_in), not from x0 / the embedding directly */
 } qres_weight_kind;
 
 #define QRES_MAX_ROWS 8    /* users (or verify rows) per step */
@@ -114,6 +118,7 @@ typedef struct {
     uint32_t* topk;         /* [rows][2 * QRES_TOPK] this rank's list: keys, then vocab indices (lm_head) */
     int32_t* out;           /* [rows][4]: greedy token, position, 0, 0 (lm_head) */
     uint16_t* mixer_out;    /* [rows][6144 / n] bf16 copy of the last layer's mixer output, or NULL */
+    const float* h_in;      /* with an fc (QRES_W_FC): [rows][5120] fp32, the hidden rows h, else NULL */
 } qres_io;
 
 typedef struct qres_ctx qres_ctx;

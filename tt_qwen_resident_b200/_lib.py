@@ -17,6 +17,7 @@ QRES_KV_BLOCK = 64
 QRES_FLAG_VERIFY = 1
 QRES_TOPK = 32
 W_GDN_IN, W_ATTN_IN, W_OUT, W_GATEUP, W_DOWN, W_HEAD = range(6)
+W_FC = 6  # the MTP draft layer fc
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "device error", 4: "out of order", 5: "communication"}
 
 # the C-ABI entry points of include/qres.h (checked by tests/test_abi.py)
@@ -104,6 +105,7 @@ class Io(ctypes.Structure):
         ("topk", ctypes.c_void_p),
         ("out", ctypes.c_void_p),
         ("mixer_out", ctypes.c_void_p),
+        ("h_in", ctypes.c_void_p),
     ]
 
 

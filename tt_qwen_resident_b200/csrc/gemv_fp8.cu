@@ -61,7 +61,9 @@ struct GemvParams {
     const uint8_t* table;   // per tile: kSelBytes row selectors, then nkb x 8 fp32 scales
     int rows, tiles, K, nkb;
     int users;              // real users (<= template B)
-    const float* x;         // PRO_RMSNORM(_ADD): fp32 [users][K]
+    const float* x;         // PRO_RMSNORM(_ADD): fp32 [users][K] (two segments: [users][seg])
+    const float* x2;        // PRO_RMSNORM over two segments: the second segment, fp32 [users][seg]
+    int seg;                // 0, or the first segment's length (K = 2 seg; rows <= 4)
     const float* red;       // PRO_RMSNORM_ADD: partials [nsrc][users][K]; x_out = x + (sum of the sources in order)
     float* x_out;           // PRO_RMSNORM_ADD: written by CTA 0
     int nsrc;               // PRO_RMSNORM_ADD: 1 (all-reduced by NCCL) or one per rank (peer exchange)
@@ -316,6 +318,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         }
     };
     auto xload = [&](int b, int i) -> float4 {
+        if (PRO == PRO_RMSNORM && p.seg) {
+            const int s4 = p.seg / 4;
+            return i < s4 ? reinterpret_cast<const float4*>(p.x + (size_t)b * p.seg)[i]
+                          : reinterpret_cast<const float4*>(p.x2 + (size_t)b * p.seg)[i - s4];
+        }
         float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
         if (PRO == PRO_RMSNORM_ADD) {
             // the sources summed in rank order first (n = 2: the same sum NCCL forms), then added to x
@@ -351,8 +358,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     // holds, straight from registers.
     constexpr bool kRegs = PRO != PRO_BF16 && B <= 2;
     constexpr int kXj = 8;
-    const bool regs = kRegs && K <= kXj * 4 * kGemvThreads;
-    float rn[B];
+    const bool regs = kRegs && K <= kXj * 4 * kGemvThreads && p.seg == 0;
+    float rn[B], rn2[B];  // rn2: the second segment's (two-segment prologue)
     if (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) {
         float4 xr[kRegs ? B : 1][kXj];
 #pragma unroll
@@ -372,11 +379,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                     }
                 } else {
+                    float ss2 = 0.f;
 #pragma unroll 5
                     for (int i = tid; i < K / 4; i += kGemvThreads) {
                         const float4 v = xload(b, i);
                         if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
-                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                        const float q = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                        if (p.seg && 4 * i >= p.seg) ss2 += q;
+                        else ss += q;
+                    }
+                    if (B <= 4) {
+                        ss2 = warp_sum(ss2);
+                        if (lane == 0) red[warp][4 + (B <= 4 ? b : 0)] = ss2;
                     }
                 }
             }
@@ -384,12 +398,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             if (lane == 0) red[warp][b] = ss;
         }
         __syncthreads();
+        const float klen = (float)(p.seg ? p.seg : K);
 #pragma unroll
         for (int b = 0; b < B; ++b) {
-            float tsum = 0.f;
+            float tsum = 0.f, tsum2 = 0.f;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) tsum += red[w][b];
-            rn[b] = rsqrt_ieee(tsum / (float)K + kEps);
+            for (int w = 0; w < 8; ++w) {
+                tsum += red[w][b];
+                if (B <= 4) tsum2 += red[w][4 + (B <= 4 ? b : 0)];
+            }
+            rn[b] = rsqrt_ieee(tsum / klen + kEps);
+            rn2[b] = rsqrt_ieee(tsum2 / klen + kEps);
         }
         if (regs) {
 #pragma unroll
@@ -411,7 +430,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         }
     } else {
 #pragma unroll
-        for (int b = 0; b < B; ++b) rn[b] = 1.f;
+        for (int b = 0; b < B; ++b) rn[b] = rn2[b] = 1.f;
     }
     // otherwise one warp per (user, K block) pair, 4 pairs in flight: lane holds K positions 4 * lane .. + 3
     const int npairs = regs ? 0 : B * nwin;
@@ -450,11 +469,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 #pragma unroll
                 for (int j = 0; j < 4; ++j) h[j] = hv[c][j];
             } else {
-                // h = bf16(x * r)
+                // h = bf16(x * r), r of the block's segment
+                int kbq = kb_start + ws;
+                if (kbq >= nkb) kbq -= nkb;
+                const bool second = p.seg && kbq * 128 >= p.seg;
                 float rb = 1.f;
 #pragma unroll
                 for (int bb = 0; bb < B; ++bb)
-                    if (bb == b) rb = rn[bb];
+                    if (bb == b) rb = second ? rn2[bb] : rn[bb];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) h[j] = bf16_round(hv[c][j] * rb);
             }
@@ -783,6 +805,10 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     if ((epi == EPI_P2P) != (e.p2p_n > 0) || (e.tagged != nullptr && pro != PRO_RMSNORM_ADD) ||
         ((e.tagged != nullptr || e.p2p_n > 0) && e.epoch == nullptr))
         return cudaErrorInvalidValue;
+    if (e.seg && (pro != PRO_RMSNORM || users > 4 || e.seg2 == nullptr || w.K != 2 * e.seg || e.seg % 128))
+        return cudaErrorInvalidValue;
+    p.x2 = e.seg2;
+    p.seg = e.seg;
     p.nsrc = e.nsrc;
     p.src_stride = e.src_stride;
     p.tagged = e.tagged;
@@ -813,6 +839,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     const size_t smem = gemv_smem_bytes(Bt, p.nkw, ns);
     if (pro == PRO_RMSNORM && epi == EPI_BF16) return launch_pe<PRO_RMSNORM, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_SILU_MUL) return launch_pe<PRO_RMSNORM, EPI_SILU_MUL>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_RMSNORM && epi == EPI_F32) return launch_pe<PRO_RMSNORM, EPI_F32>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_BF16) return launch_pe<PRO_RMSNORM_ADD, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_SILU_MUL) return launch_pe<PRO_RMSNORM_ADD, EPI_SILU_MUL>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_RESID) return launch_pe<PRO_BF16, EPI_RESID>(p, Bt, grid, smem, st, pdl);

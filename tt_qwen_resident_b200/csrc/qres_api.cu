@@ -138,6 +138,8 @@ struct qres_ctx {
     std::vector<Layer> layers;
     qres_weight head = {};
     bool has_head = false;
+    qres_weight fc = {};  // the MTP draft layer's fc (QRES_W_FC)
+    bool has_fc = false;
     const float *cos_tab = nullptr, *sin_tab = nullptr;
     int max_pos = 0;
     qres_io io = {};
@@ -146,7 +148,7 @@ struct qres_ctx {
     uint8_t* ws = nullptr;
     size_t ws_bytes = 0;
     uint32_t* err = nullptr;
-    float *xb = nullptr, *partial = nullptr;
+    float *xb = nullptr, *xe = nullptr, *partial = nullptr;
     uint16_t *y = nullptr, *o = nullptr, *a = nullptr;
     int32_t* argmax = nullptr;
     uint32_t* gathered = nullptr;
@@ -201,7 +203,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, epoch, xb, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
+    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -216,6 +218,7 @@ Carve carve(const qres_ctx* c) {
     k.err = take(256);
     k.epoch = take(256);
     k.xb = take((size_t)R * kHidden * 4);
+    k.xe = take((size_t)R * kHidden * 4);
     k.partial = take((size_t)R * kHidden * 4);
     k.y = take((size_t)R * c->ld_y * 2);
     k.o = take((size_t)R * c->gv * 2);
@@ -306,6 +309,15 @@ qres_status qres_destroy(qres_ctx* ctx) {
 
 qres_status qres_load_weights(qres_ctx* c, int32_t layer, int32_t kind, const qres_weight* w) {
     if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    if (kind == QRES_W_FC) {
+        // the MTP draft layer's fc (K = the embedding row | the hidden row); one rank only
+        if (c->nranks != 1) return fail(c, QRES_ERR_ARG, "the fc (MTP draft layer) runs on one rank");
+        qres_status s = check_weight(c, w, kHidden, 2 * kHidden, "fc");
+        if (s) return s;
+        c->fc = *w;
+        c->has_fc = true;
+        return QRES_OK;
+    }
     if (kind == QRES_W_HEAD) {
         if (!c->vocab_local) return fail(c, QRES_ERR_ARG, "lm_head bound but vocab is 0");
         qres_status s = check_weight(c, w, c->vocab_local, kHidden, "lm_head");
@@ -397,6 +409,7 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->err = reinterpret_cast<uint32_t*>(w + k.err);
     c->epoch = reinterpret_cast<uint32_t*>(w + k.epoch);
     c->xb = reinterpret_cast<float*>(w + k.xb);
+    c->xe = reinterpret_cast<float*>(w + k.xe);
     c->partial = reinterpret_cast<float*>(w + k.partial);
     c->y = reinterpret_cast<uint16_t*>(w + k.y);
     c->o = reinterpret_cast<uint16_t*>(w + k.o);
@@ -489,6 +502,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     const int verify = (c->cfg.flags & QRES_FLAG_VERIFY) ? R : 0;
     const P2PLayout pl(R);
     if (c->cfg.vocab && !c->has_head) return fail(c, QRES_ERR_STATE, "lm_head not loaded");
+    if (c->has_fc && (!c->io.h_in || R > 4)) return fail(c, QRES_ERR_STATE, "the fc needs io.h_in (and at most 4 rows)");
     for (int l = 0; l < c->cfg.layers; ++l) {
         const Layer& L = c->layers[l];
         const bool at = is_attn(c, l);
@@ -498,7 +512,13 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (at ? (!L.wq || !c->cos_tab || !c->io.page_table) : (!L.taps))
             return fail(c, QRES_ERR_STATE, "layer %d: parameters not bound", l);
     }
-    const int grid = 2 * c->sm_count;  // two weight-streaming CTAs per SM
+    // weight-streaming CTAs per projection: two per SM, fewer for a small one (a tensor-parallel shard) so that
+    // each CTA streams at least ~4 units of 16 KB -- every CTA pays a fixed prologue (reading the whole
+    // residual, with the peer exchange one copy per rank), which the small shards' few units do not amortise
+    auto grid_of = [&](const qres_weight& w) {
+        const int units = (w.rows_pad / 128) * (w.K / 128);
+        return std::max(c->sm_count / 2, std::min(2 * c->sm_count, units / 4));
+    };
     const int32_t* pos = c->io.tok->pos;
     int launches = 0;
     auto K = [&](cudaError_t e, const char* what) -> qres_status {
@@ -513,7 +533,9 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     } while (0)
     float* cur = c->io.x;  // residual stream
     float* other = c->xb;
-    STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
+    if (!c->has_fc) {
+        STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
+    }
     bool pending = false;  // all-reduced partials waiting to be added to cur
     int xchg = 0;          // row-parallel exchanges issued so far in this step (peer exchange: slot xchg % 2)
     auto allreduce = [&]() -> qres_status {
@@ -541,7 +563,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     const int kPrefetchUnits = 2;  // 32 KB per CTA
     auto gemv = [&](const qres_weight& w, int pro, const void* in, int ld_in, int epi, void* out, int ld_out,
                     const float* red, float* x_out, const char* what) -> qres_status {
-        return K(gemv_launch(w, R, pro, in, ld_in, epi, out, ld_out, grid, c->err, st, true, red, x_out, c->gemv_work,
+        return K(gemv_launch(w, R, pro, in, ld_in, epi, out, ld_out, grid_of(w), c->err, st, true, red, x_out, c->gemv_work,
                              c->gemv_work_bytes, next_of(&w), kPrefetchUnits),
                  what);
     };
@@ -555,7 +577,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             ex.epoch = c->epoch;
             ex.tag_mul = 2u * (uint32_t)c->cfg.layers;
             ex.tag_add = (uint32_t)j + 1u;
-            qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid, c->err, st, true,
+            qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true,
                                           reinterpret_cast<const float*>(ex.tagged), other, c->gemv_work,
                                           c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
                               what);
@@ -584,7 +606,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             ex.tag_add = (uint32_t)xchg + 1u;
             for (int r = 0; r < n; ++r)
                 ex.peer_data[r] = reinterpret_cast<uint2*>(c->p2p_peer[r] + pl.data) + ((size_t)slot * 8 + c->rank) * R * kHidden;
-            qres_status s = K(gemv_launch(w, R, 1, in, w.K, 4, nullptr, kHidden, grid, c->err, st, true, nullptr,
+            qres_status s = K(gemv_launch(w, R, 1, in, w.K, 4, nullptr, kHidden, grid_of(w), c->err, st, true, nullptr,
                                           nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
                               what);
             ++xchg;
@@ -597,6 +619,18 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         pending = true;
         return s;
     };
+    if (c->has_fc) {
+        // the MTP draft layer's input (mtp.py:1-14, streamer_compute.cpp:424-435): x = fc([rmsnorm(e) |
+        // rmsnorm(h)]) for e = the token's embedding row and h = io.h_in (a previous step's last x); the pre-fc
+        // norm weights are folded into the fc's columns; no residual
+        STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, c->xe, R, c->err, st, true), "rows in");
+        GemvExchange ex;
+        ex.seg = kHidden;
+        ex.seg2 = c->io.h_in;
+        STEP(gemv_launch(c->fc, R, 0, c->xe, kHidden, 3, cur, kHidden, grid_of(c->fc), c->err, st, true, nullptr, nullptr,
+                         c->gemv_work, c->gemv_work_bytes, nullptr, 0, &ex),
+             "fc");
+    }
     for (int l = 0; l < c->cfg.layers; ++l) {
         const Layer& L = c->layers[l];
         const bool at = is_attn(c, l);

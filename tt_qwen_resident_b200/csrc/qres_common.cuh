@@ -133,6 +133,11 @@ struct GemvExchange {
     int p2p_n = 0;                     // epilogue: destinations (ranks)
     int peer_ld = 0;                   // words per user row in a destination region
     uint2* peer_data[8] = {};          // this rank's region in each rank's window
+    // the rmsnorm prologue over two segments (the MTP fc, mtp.py:54-60 / streamer_common.hpp fc): K = 2 seg,
+    // positions [0, seg) from the launch's input (fp32 [users][seg]), [seg, 2 seg) from seg2, each segment
+    // normalised on its own; seg 0 = one segment
+    const float* seg2 = nullptr;
+    int seg = 0;
 };
 
 // destinations of a small per-step peer exchange, double-buffered by step parity: this rank's region in each

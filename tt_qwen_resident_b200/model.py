@@ -55,6 +55,7 @@ class ResidentModel:
         nccl_id=None,
         p2p=False,
         verify=False,
+        fc=None,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
@@ -109,6 +110,14 @@ class ResidentModel:
         self.w_gu = [shard(stack_matrices(m["G"], m["U"]), d.gateup_rows()) for m in w["mlp"]]
         self.w_down = [shard(m["D"], None, d.mlp_k()) for m in w["mlp"]]
         self.w_head = shard(w["head"], d.vocab_rows()) if self.lm_head else None
+        # the MTP draft layer (mtp.py:1-14): layer 0's residual is fc([rmsnorm(e) | rmsnorm(h)]), e the token's
+        # embedding row, h the rows of h_d (set_hidden: a previous step's last x); fc canonical [5120, 10240]
+        # FP8 with the pre-fc norm weights folded into its columns
+        if fc is not None:
+            assert nranks == 1, "the fc (MTP draft layer) runs on one rank"
+            self.w_fc = shard(fc)
+        else:
+            self.w_fc = None
         self.weight_bytes = self._count_weight_bytes()
         # ---- decode state (per state copy)
         R = batch
@@ -131,6 +140,7 @@ class ResidentModel:
         self.topk_d = torch.zeros(R, 2 * TOP_K, dtype=torch.int32, device=dev)
         self.out_d = torch.zeros(R, 4, dtype=torch.int32, device=dev)
         self.mixer_d = torch.zeros(R, d.gv, dtype=torch.bfloat16, device=dev)
+        self.h_d = torch.zeros(R, HIDDEN, device=dev)  # the fc's hidden rows (MTP draft layer)
         self.embed = embed.to(dev).bfloat16().contiguous() if embed is not None else None
         cos, sin = rope_table(max_pos)
         self.cos_d, self.sin_d = cos.to(dev), sin.to(dev)
@@ -200,6 +210,8 @@ class ResidentModel:
             _lib.check(L.qres_load_weights(c, l, _lib.W_DOWN, ctypes.byref(self.w_down[m].cstruct())), c, "w down")
         if self.lm_head:
             _lib.check(L.qres_load_weights(c, -1, _lib.W_HEAD, ctypes.byref(self.w_head.cstruct())), c, "w head")
+        if self.w_fc is not None:
+            _lib.check(L.qres_load_weights(c, -1, _lib.W_FC, ctypes.byref(self.w_fc.cstruct())), c, "w fc")
         _lib.check(L.qres_bind_rope(c, _lib.ptr(self.cos_d), _lib.ptr(self.sin_d), self.max_pos), c, "rope")
         io = _lib.Io(
             self.tok_d.data_ptr(),
@@ -211,8 +223,16 @@ class ResidentModel:
             self.topk_d.data_ptr() if self.lm_head else 0,
             self.out_d.data_ptr() if self.lm_head else 0,
             self.mixer_d.data_ptr(),
+            self.h_d.data_ptr() if self.w_fc is not None else 0,
         )
         _lib.check(L.qres_bind_io(c, ctypes.byref(io)), c, "io")
+
+    def set_hidden(self, h, stream=None):
+        """the hidden rows the next step's fc reads (MTP draft layer): a [rows, 5120] fp32 device tensor, e.g.
+        the main model's x_d or this model's own (copied, so the step may overwrite its source)"""
+        s = stream or torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(s):
+            self.h_d.copy_(h.reshape(self.batch, HIDDEN), non_blocking=True)
 
     def _count_weight_bytes(self):
         """algorithmic weight bytes one step streams on this rank (FP8 + 4 B per 128x128 block)"""
