@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--chain", action="store_true",
+                    help="the chained projections between two mixers (one persistent launch) instead of one launch each")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel exchange: the fused NVLink peer exchange (default) or NCCL (baseline)")
     return ap.parse_args()
@@ -235,7 +237,8 @@ def run_ours(args, rank, world, local):
     w = weights.random_canonical(layers, INTERVAL, VOCAB, seed=0, device=dev)
     emb = torch.randn(VOCAB, 5120, generator=torch.Generator(device=dev).manual_seed(1), device=dev).bfloat16()
     model = ResidentModel(w, layers, INTERVAL, batch=batch, max_pos=max_pos, lm_head=True, embed=emb, rank=rank,
-                          nranks=world, nccl_id=nid, p2p=world > 1 and args.exchange == "p2p", device=dev)
+                          nranks=world, nccl_id=nid, p2p=world > 1 and args.exchange == "p2p", device=dev,
+                          chain=args.chain)
     del w
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t_build
@@ -339,6 +342,7 @@ def run_ours(args, rank, world, local):
                 "prompt": prompt,
                 "layers": layers,
                 "parallelism": f"tp{world}",
+                "projections": "chained between mixers (gemv_chain)" if args.chain else "per-projection launches",
                 "exchange": ("fused NVLink peer exchange in the GEMV epilogue" if args.exchange == "p2p" else "NCCL")
                 if world > 1 else None,
                 "l2": "inputs larger than L2 (25.6 GB of weights streamed per step)",

@@ -20,7 +20,7 @@
 #include <string>
 #include <vector>
 
-#include "qres_common.cuh"
+#include "gemv_chain.cuh"
 
 namespace qres {
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
@@ -106,14 +106,14 @@ bool load_nccl(const char* libpath, std::string* why) {
 
 // A rank's peer-exchange window (qres_p2p_*): one cudaMalloc allocation, mapped into every other rank with
 // CUDA IPC. Layout: list counters [2 slots][8 source ranks] (uint32, 256-byte header), then the row-parallel
-// partials [2 slots][8 sources][rows][5120] as tagged words {fp32 bits, tag}, then the top-32 lists
+// partials [3 slots][8 sources][rows][5120] as tagged words {fp32 bits, tag}, then the top-32 lists
 // [2 slots][8 sources][rows][64] uint32. Row-parallel exchange j of step s uses slot j % 2 and tag
 // s * 2L + j + 1 (L layers; never 0, so the zeroed window holds no valid word); step s's lists use slot s % 2 and
 // their counters only grow (the k-th use of a slot completes at k).
 struct P2PLayout {
     size_t lcnt = 0, data = 256, lists = 0, total = 0;
     explicit P2PLayout(int rows) {
-        lists = data + (size_t)2 * 8 * rows * kHidden * 8;
+        lists = data + (size_t)3 * 8 * rows * kHidden * 8;
         total = lists + (size_t)2 * 8 * rows * 2 * QRES_TOPK * 4;
     }
 };
@@ -159,6 +159,9 @@ struct qres_ctx {
     int topk_blk = 1;
     void* gemv_work = nullptr;
     size_t gemv_work_bytes = 0;
+    uint2 *xch = nullptr, *atag = nullptr;
+    void* chain_work = nullptr;
+    size_t chain_work_bytes = 0;
     ncclComm_t comm = nullptr;
     // peer exchange (qres_p2p_alloc / qres_p2p_open): this rank's window and every rank's window as mapped here
     uint8_t* p2p_local = nullptr;
@@ -203,7 +206,8 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, total;
+    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, xch, atag, chain,
+        chain_bytes, total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -229,6 +233,12 @@ Carve carve(const qres_ctx* c) {
     k.topk = take(c->vocab_local ? topk_workspace_bytes(R, c->topk_blk) : 0);
     k.gemv_bytes = gemv_workspace_bytes(2 * c->sm_count);
     k.gemv = take(k.gemv_bytes);
+    // the chained projections (gemv_chain.cu): the one-rank exchange slots [3][rows][5120] and gate|up's tagged
+    // SwiGLU output [rows][17408 / n], as tagged 8-byte words, and the chain's tickets / partial sums
+    k.xch = take((size_t)3 * R * kHidden * 8);
+    k.atag = take((size_t)R * c->ic * 8);
+    k.chain_bytes = chain_workspace_bytes(2 * c->sm_count);
+    k.chain = take(k.chain_bytes);
     k.total = off;
     return k;
 }
@@ -266,7 +276,8 @@ qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qr
     if (cfg->rows < 1 || cfg->rows > QRES_MAX_ROWS || cfg->layers < 1)
         return fail(nullptr, QRES_ERR_ARG, "qres_create: rows %d, layers %d", cfg->rows, cfg->layers);
     if (cfg->vocab % nranks) return fail(nullptr, QRES_ERR_ARG, "qres_create: vocab %d not divisible by %d", cfg->vocab, nranks);
-    if (cfg->flags & ~QRES_FLAG_VERIFY) return fail(nullptr, QRES_ERR_ARG, "qres_create: unknown flags %#x", cfg->flags);
+    if (cfg->flags & ~(QRES_FLAG_VERIFY | QRES_FLAG_CHAIN))
+        return fail(nullptr, QRES_ERR_ARG, "qres_create: unknown flags %#x", cfg->flags);
     if ((cfg->flags & QRES_FLAG_VERIFY) && (cfg->rows < 2 || cfg->rows + 3 > QRES_HIST_SLOTS))
         return fail(nullptr, QRES_ERR_ARG, "qres_create: a verify step has 2..%d rows, not %d", QRES_HIST_SLOTS - 3,
                     cfg->rows);
@@ -421,6 +432,10 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->topk_work = c->vocab_local ? (void*)(w + k.topk) : nullptr;
     c->gemv_work = w + k.gemv;
     c->gemv_work_bytes = k.gemv_bytes;
+    c->xch = reinterpret_cast<uint2*>(w + k.xch);
+    c->atag = reinterpret_cast<uint2*>(w + k.atag);
+    c->chain_work = w + k.chain;
+    c->chain_work_bytes = k.chain_bytes;
     return QRES_OK;
 }
 
@@ -536,6 +551,8 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     if (!c->has_fc) {
         STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
     }
+    // the chained projections (gemv_chain.cu): with an lm_head, and the peer exchange when nranks > 1
+    const bool chain = c->cfg.vocab > 0 && (c->cfg.flags & QRES_FLAG_CHAIN) && (!tp || p2p) && R <= 4;
     bool pending = false;  // all-reduced partials waiting to be added to cur
     int xchg = 0;          // row-parallel exchanges issued so far in this step (peer exchange: slot xchg % 2)
     auto allreduce = [&]() -> qres_status {
@@ -635,8 +652,11 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         const Layer& L = c->layers[l];
         const bool at = is_attn(c, l);
         uint16_t* mcopy = (l == c->cfg.layers - 1) ? c->io.mixer_out : nullptr;
-        qres_status s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
-        if (s) return s;
+        qres_status s = QRES_OK;
+        if (!chain || l == 0) {  // chained: layers > 0 get theirs from the previous chain
+            s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
+            if (s) return s;
+        }
         // the mixer is latency-bound: it pulls the whole out-projection into L2 meanwhile
         const void* pf = L.w[QRES_W_OUT].data;
         const size_t pf_bytes = (size_t)L.w[QRES_W_OUT].rows_pad * L.w[QRES_W_OUT].K;
@@ -650,6 +670,71 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                             c->o, mcopy, c->err, st, true, pf, pf_bytes, verify, &c->io.tok->slot),
                  "gdn");
         }
+        if (chain) {
+            // out-proj, gate|up, down and the next in-proj (or the lm_head) as one persistent launch; exchange j of
+            // the step (out 2l, down 2l + 1) carries tag epoch * 2L + j + 1, gate|up's output epoch * L + l + 1
+            const int L2 = 2 * c->cfg.layers;
+            ChainParams cp = {};
+            cp.nphase = 4;
+            cp.users = R;
+            cp.nsrc = n;
+            cp.epoch = c->epoch;
+            cp.rank = c->rank;
+            cp.set_mul = (uint32_t)L2;
+            cp.src_words = (size_t)R * kHidden;
+            cp.slot_words = (size_t)(p2p ? 8 : 1) * R * kHidden;
+            for (int r = 0; r < n; ++r) cp.xbase[r] = p2p ? reinterpret_cast<uint2*>(c->p2p_peer[r] + pl.data) : c->xch;
+            auto phase = [&](ChainPhase& ph, const qres_weight& w) {
+                ph.w = static_cast<const uint8_t*>(w.data);
+                ph.table = reinterpret_cast<const uint8_t*>(w.uscale);
+                ph.rows = w.rows;
+                ph.tiles = w.rows_pad / 128;
+                ph.K = w.K;
+                ph.nkb = w.K / 128;
+            };
+            ChainPhase& po = cp.ph[0];
+            phase(po, L.w[QRES_W_OUT]);
+            po.in_kind = CIN_BF16;
+            po.in_bf16 = c->o;
+            po.out_kind = COUT_PARTIAL;
+            po.ld_out = kHidden;
+            po.out_add = (uint32_t)(2 * l + 1);
+            ChainPhase& pg = cp.ph[1];
+            phase(pg, L.w[QRES_W_GATEUP]);
+            pg.in_kind = CIN_NORM;
+            pg.x = cur;
+            pg.nsets = 1;
+            pg.set_add[0] = (uint32_t)(2 * l + 1);
+            pg.out_kind = COUT_SILU_TAGGED;
+            pg.out = c->atag;
+            pg.ld_out = c->ic;
+            pg.out_mul = (uint32_t)c->cfg.layers;
+            pg.out_add = (uint32_t)(l + 1);
+            ChainPhase& pd = cp.ph[2];
+            phase(pd, L.w[QRES_W_DOWN]);
+            pd.in_kind = CIN_TAGGED_BF16;
+            pd.in_tagged = c->atag;
+            pd.in_mul = (uint32_t)c->cfg.layers;
+            pd.in_add = (uint32_t)(l + 1);
+            pd.out_kind = COUT_PARTIAL;
+            pd.ld_out = kHidden;
+            pd.out_add = (uint32_t)(2 * l + 2);
+            ChainPhase& pn = cp.ph[3];
+            const bool last = l == c->cfg.layers - 1;
+            phase(pn, last ? c->head : c->layers[l + 1].w[is_attn(c, l + 1) ? QRES_W_ATTN_IN : QRES_W_GDN_IN]);
+            pn.in_kind = CIN_NORM;
+            pn.x = cur;
+            pn.nsets = 2;
+            pn.set_add[0] = (uint32_t)(2 * l + 1);
+            pn.set_add[1] = (uint32_t)(2 * l + 2);
+            pn.x_out = other;
+            pn.out_kind = COUT_BF16;
+            pn.out = last ? static_cast<void*>(c->io.logits) : static_cast<void*>(c->y);
+            pn.ld_out = last ? c->vocab_local : c->ld_y;
+            STEP(chain_launch(cp, 2 * c->sm_count, c->sm_count, c->chain_work, c->chain_work_bytes, st, true), "chain");
+            std::swap(cur, other);
+            continue;
+        }
         s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");
         if (s) return s;
         s = norm_gemv(L.w[QRES_W_GATEUP], 1, c->a, c->ic, "gate-up");
@@ -658,8 +743,10 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (s) return s;
     }
     if (c->cfg.vocab) {
-        qres_status s = norm_gemv(c->head, 0, c->io.logits, c->vocab_local, "lm_head");
-        if (s) return s;
+        if (!chain) {
+            qres_status s = norm_gemv(c->head, 0, c->io.logits, c->vocab_local, "lm_head");
+            if (s) return s;
+        }
         const int base = c->rank * c->vocab_local;
         if (!tp) {
             STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, c->argmax, c->topk_work,

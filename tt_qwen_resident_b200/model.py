@@ -56,6 +56,7 @@ class ResidentModel:
         p2p=False,
         verify=False,
         fc=None,
+        chain=False,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
@@ -83,8 +84,10 @@ class ResidentModel:
         gc, ac = state_copies or (self.n_gdn, self.n_attn)
         self.state_copies = (max(gc, 1) if self.n_gdn else 0, max(ac, 1) if self.n_attn else 0)
         L = _lib.lib()
-        cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count,
-                          _lib.QRES_FLAG_VERIFY if self.verify else 0)
+        # chain: the projections between two mixers as one persistent launch (gemv_chain.cu) where the library
+        # can (lm_head, <= 4 rows, peer exchange when nranks > 1); False (default): one launch per projection
+        flags = (_lib.QRES_FLAG_VERIFY if self.verify else 0) | (_lib.QRES_FLAG_CHAIN if chain else 0)
+        cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count, flags)
         h = ctypes.c_void_p()
         _lib.check(L.qres_create(ctypes.byref(cfg), rank, nranks, ctypes.byref(h)), None, "qres_create")
         self.ctx = h
