@@ -84,6 +84,48 @@ __device__ __forceinline__ void rms_rope_head(const uint16_t* src, const float* 
     __syncthreads();
 }
 
+// the G query heads of a group at once (256 threads, one dim each): dst[j] = rope(rmsnorm(src_j) * w), fp32; all
+// loads in flight together and one reduction round for every head
+__device__ __forceinline__ void rms_rope_group(const uint16_t* src, int G, const float* w, const float* cs,
+                                               const float* sn, float (*dst)[kHD], float (*red)[kMaxGroup]) {
+    const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+    float v[kMaxGroup];
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) v[j] = j < G ? __uint_as_float((uint32_t)src[(size_t)j * kHD + d] << 16) : 0.f;
+    const float wd = w[d];
+    float c = 0.f, s = 0.f;
+    if (d < kRot / 2) {
+        c = cs[d];
+        s = sn[d];
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) {
+        const float ss = warp_sum(v[j] * v[j]);
+        if (lane == 0) red[warp][j] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) {
+        if (j >= G) break;
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t += red[i][j];
+        const float r = rsqrt_ieee(t / (float)kHD + kEps);
+        dst[j][d] = mul_rn(mul_rn(v[j], r), wd);
+    }
+    __syncthreads();
+    if (d < kRot / 2) {
+#pragma unroll
+        for (int j = 0; j < kMaxGroup; ++j) {
+            if (j >= G) break;
+            const float a = dst[j][d], b = dst[j][d + kRot / 2];
+            dst[j][d] = mul_rn(a, c) - mul_rn(b, s);
+            dst[j][d + kRot / 2] = mul_rn(b, c) + mul_rn(a, s);
+        }
+    }
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;  // [2][K page | V page]
@@ -124,6 +166,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const int npg = (L + kKvBlock - 1) / kKvBlock;
     const int ppc = (npg + p.nchunks - 1) / p.nchunks;
     const int pg0 = c * ppc, pg1 = min(pg0 + ppc, npg);
+    // chunks that hold pages at this length: the others leave at once (no partial, no ticket), so a short
+    // context costs what its pages do
+    const int nce = (npg + ppc - 1) / ppc;
+    if (c >= nce) return;
     const int* pt = p.page_table + (size_t)(p.verify ? 0 : b) * p.max_pages;
     const uint16_t* y = p.y + (size_t)b * p.ld_y;
     const float* cs = p.cos_tab + (size_t)pos * (kRot / 2);
@@ -152,9 +198,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
         for (int i = 0; i < min(npages, 2); ++i) issue(i, i);
     }
 
-    // q of the group's heads (fp32)
-    for (int j = 0; j < G; ++j)
-        rms_rope_head(y + (size_t)(g * G + j) * kHD, p.wq, cs, sn, qf[j], red, false);
+    // q of the group's heads (fp32), all heads in one pass
+    {
+        __shared__ float redg[8][kMaxGroup];
+        rms_rope_group(y + (size_t)(g * G) * kHD, G, p.wq, cs, sn, qf, redg);
+    }
     // k / v of the new positions p0 .. pos whose pages this CTA covers (row j's from its own y row)
     const int kbase = 2 * p.h * kHD;
     const int pg_lo = pg0 * kKvBlock, pg_hi = pg1 * kKvBlock;  // positions of this CTA's pages
@@ -290,7 +338,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     if (tid == 0) {
         __threadfence();
         const int t = atomicAdd(p.ticket + b * p.nkv + g, 1);
-        last_flag = (t == p.nchunks - 1);
+        last_flag = (t == nce - 1);
         if (last_flag) __threadfence();
     }
     __syncthreads();
@@ -300,13 +348,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     // independent loads.
     const float* base = p.part + (((size_t)b * p.nkv + g) * p.nchunks) * G * (2 + kHD);
     float* wch = reinterpret_cast<float*>(ring);  // [nchunks][G] chunk weights (the K/V ring is free now)
-    for (int i = tid; i < p.nchunks * G; i += kAttnThreads) wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
+    for (int i = tid; i < nce * G; i += kAttnThreads) wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
     __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
-        for (int cc = 0; cc < p.nchunks; ++cc) M = fmaxf(M, wch[cc * G + tid]);
+        for (int cc = 0; cc < nce; ++cc) M = fmaxf(M, wch[cc * G + tid]);
         float Lsum = 0.f;
-        for (int cc = 0; cc < p.nchunks; ++cc) {
+        for (int cc = 0; cc < nce; ++cc) {
             const float mc = wch[cc * G + tid];
             const float w = mc == -INFINITY ? 0.f : expf(mc - M);
             wch[cc * G + tid] = w;
@@ -318,9 +366,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     for (int j = 0; j < G; ++j) {
         float O = 0.f;
 #pragma unroll 8
-        for (int cc = 0; cc < p.nchunks; ++cc) {
-            const float w = wch[cc * G + j];
-            if (w != 0.f) O = fmaf(w, __ldcg(base + ((size_t)cc * G + j) * (2 + kHD) + 2 + tid), O);
+        // chunk weights applied in chunk order; the loads of 4 chunks in flight at once
+        for (int cc = 0; cc < nce; cc += 4) {
+            float ov[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                ov[u] = cc + u < nce ? __ldcg(base + ((size_t)(cc + u) * G + j) * (2 + kHD) + 2 + tid) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float w = cc + u < nce ? wch[(cc + u) * G + j] : 0.f;
+                if (w != 0.f) O = fmaf(w, ov[u], O);
+            }
         }
         const int hq = g * G + j;
         const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);

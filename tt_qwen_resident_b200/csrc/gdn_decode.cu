@@ -89,6 +89,22 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
         const float* S0 = p.state + (((size_t)b * p.nv + hh) * kDK) * kDV + c0;
         bulk_prefetch_l2(S0 + (size_t)tid * kDV, kGdnCols * 4);
     }
+    // the conv taps (immutable) and every slot of this CTA's conv-history channels (written only by this kernel,
+    // a step earlier) into L2 as well: q and k of the key head (2 x 256 B per slot), v of the CTA's 32 columns
+    if (tid >= kDK - 3 * 8 && tid < kDK) {
+        const int i = tid - (kDK - 3 * 8);  // 24 threads: 8 slots x (q, k, v)
+        const int slot = i / 3, part = i % 3;
+        const uint16_t* h = p.hist + ((size_t)(R ? 0 : b) * QRES_HIST_SLOTS + slot) * conv;
+        const size_t ch = part == 0 ? (size_t)kh * kDK : part == 1 ? (size_t)gq + kh * kDK : (size_t)2 * gq + hh * kDV + c0;
+        const uint32_t bytes = part == 2 ? kGdnCols * 2 : kDK * 2;
+        // 16-byte aligned starts and sizes (channel offsets are multiples of 32)
+        bulk_prefetch_l2(h + ch, bytes);
+    }
+    if (tid == 0) {
+        bulk_prefetch_l2(p.taps + (size_t)kh * kDK * 4, kDK * 8);
+        bulk_prefetch_l2(p.taps + ((size_t)gq + kh * kDK) * 4, kDK * 8);
+        bulk_prefetch_l2(p.taps + ((size_t)2 * gq + hh * kDV + c0) * 4, kGdnCols * 8);
+    }
     // the following projection's weights (immutable) stream into L2 meanwhile: this kernel is latency-bound
     if (p.pf && tid == 0) {
         const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
@@ -116,32 +132,42 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
                    (size_t)hh * kDK * kDV + c0;
         if (!bad) {
             const int swr = pos % QRES_HIST_SLOTS;
-            // ---- conv1d + SiLU: q, k of the key head (256 channels) and this CTA's 32 v channels
-            for (int i = tid; i < 2 * kDK + kGdnCols; i += kGdnThreads) {
-                int ch, which;
-                if (i < kDK) {
-                    ch = kh * kDK + i;
-                    which = 0;
-                } else if (i < 2 * kDK) {
-                    ch = gq + kh * kDK + (i - kDK);
-                    which = 1;
-                } else {
-                    ch = 2 * gq + hh * kDV + c0 + (i - 2 * kDK);
-                    which = 2;
+            // ---- conv1d + SiLU: q, k of the key head (256 channels) and this CTA's 32 v channels; a thread's
+            // (up to 3) channels have all their loads in flight before any arithmetic
+            constexpr int kIt = (2 * kDK + kGdnCols + kGdnThreads - 1) / kGdnThreads;  // 3
+            uint16_t yin[kIt], hw[kIt][3];
+            uint2 tp[kIt];
+            int chs[kIt];
+#pragma unroll
+            for (int it = 0; it < kIt; ++it) {
+                const int i = tid + it * kGdnThreads;
+                chs[it] = -1;
+                if (i < 2 * kDK + kGdnCols) {
+                    const int ch = i < kDK ? kh * kDK + i
+                                           : i < 2 * kDK ? gq + kh * kDK + (i - kDK) : 2 * gq + hh * kDV + c0 + (i - 2 * kDK);
+                    chs[it] = ch;
+                    yin[it] = y[ch];
+                    // window positions pos-3 .. pos-1: from the ring below p0, from this step's rows from p0 on
+#pragma unroll
+                    for (int jj = 0; jj < 3; ++jj) {
+                        const int q = pos - 3 + jj;
+                        hw[it][jj] = q >= p0 && R ? p.y[(size_t)(q - p0) * p.ld_y + ch]
+                                                  : hist[(size_t)((q + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv + ch];
+                    }
+                    tp[it] = *reinterpret_cast<const uint2*>(p.taps + (size_t)ch * 4);
                 }
-                const uint16_t yin = y[ch];
-                // window positions pos-3 .. pos: from the ring below p0, from this step's rows from p0 on
+            }
+#pragma unroll
+            for (int it = 0; it < kIt; ++it) {
+                const int i = tid + it * kGdnThreads;
+                if (chs[it] < 0) continue;
+                const int ch = chs[it];
+                const int which = i < kDK ? 0 : i < 2 * kDK ? 1 : 2;
                 float w[4];
 #pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    const int q = pos - 3 + j;
-                    const uint16_t hv = q >= p0 && R ? p.y[(size_t)(q - p0) * p.ld_y + ch]
-                                                     : hist[(size_t)((q + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv + ch];
-                    w[j] = __uint_as_float((uint32_t)hv << 16);
-                }
-                w[3] = __uint_as_float((uint32_t)yin << 16);
-                const uint2 tp = *reinterpret_cast<const uint2*>(p.taps + (size_t)ch * 4);
-                const float t0 = bf16lo(tp.x), t1 = bf16hi(tp.x), t2 = bf16lo(tp.y), t3 = bf16hi(tp.y);
+                for (int jj = 0; jj < 3; ++jj) w[jj] = __uint_as_float((uint32_t)hw[it][jj] << 16);
+                w[3] = __uint_as_float((uint32_t)yin[it] << 16);
+                const float t0 = bf16lo(tp[it].x), t1 = bf16hi(tp[it].x), t2 = bf16lo(tp[it].y), t3 = bf16hi(tp[it].y);
                 float acc = mul_rn(w[0], t0);
                 acc = add_rn(acc, mul_rn(w[1], t1));
                 acc = add_rn(acc, mul_rn(w[2], t2));
@@ -152,7 +178,7 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
                 else vv[i - 2 * kDK] = c;
                 // one writer per history element: the key head's first value head, quarter 0, for q / k; every
                 // quarter for its v columns
-                if (which == 2 || (hh % group == 0 && qtr == 0)) hist[swr * conv + ch] = yin;
+                if (which == 2 || (hh % group == 0 && qtr == 0)) hist[swr * conv + ch] = yin[it];
             }
         }
         __syncthreads();
