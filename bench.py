@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--tile-finish", action="store_true",
+                    help="finish split projection tiles by ticket instead of the fixed-point accumulators (1 rank)")
     ap.add_argument("--chain", action="store_true",
                     help="the chained projections between two mixers (one persistent launch) instead of one launch each")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -238,7 +240,7 @@ def run_ours(args, rank, world, local):
     emb = torch.randn(VOCAB, 5120, generator=torch.Generator(device=dev).manual_seed(1), device=dev).bfloat16()
     model = ResidentModel(w, layers, INTERVAL, batch=batch, max_pos=max_pos, lm_head=True, embed=emb, rank=rank,
                           nranks=world, nccl_id=nid, p2p=world > 1 and args.exchange == "p2p", device=dev,
-                          chain=args.chain)
+                          chain=args.chain, tile_finish=args.tile_finish)
     del w
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t_build
@@ -343,6 +345,8 @@ def run_ours(args, rank, world, local):
                 "layers": layers,
                 "parallelism": f"tp{world}",
                 "projections": "chained between mixers (gemv_chain)" if args.chain else "per-projection launches",
+                "split_tiles": ("fixed-point accumulators" if world == 1 and batch <= 2 and not args.chain
+                                and not args.tile_finish else "finished by ticket"),
                 "exchange": ("fused NVLink peer exchange in the GEMV epilogue" if args.exchange == "p2p" else "NCCL")
                 if world > 1 else None,
                 "l2": "inputs larger than L2 (25.6 GB of weights streamed per step)",

@@ -64,7 +64,7 @@ typedef struct {
     int32_t max_pages;     /* page-table entries per user */
     int32_t num_pages;     /* pages in each attention layer's K (and V) pool */
     int32_t sm_count;      /* SMs to use; 0 = the device's (the weight-streaming kernels run 2 CTAs per SM) */
-    int32_t flags;         /* QRES_FLAG_VERIFY, or 0 */
+    int32_t flags;         /* QRES_FLAG_VERIFY | QRES_FLAG_CHAIN | QRES_FLAG_TILE_FINISH, or 0 */
 } qres_config;
 
 /* qres_config.flags: the verify step (ResidentModel(verify=True), model.py:416-457): the `rows` rows (2..5) are
@@ -79,11 +79,18 @@ typedef struct {
  * nranks > 1, the peer exchange; otherwise the per-projection path runs. Off by default: on B200 at one rank it
  * measured 4% slower than the per-projection launches (7.83 vs 7.52 ms per step). */
 #define QRES_FLAG_CHAIN 2
+/* qres_config.flags: at one rank, with an lm_head and up to 2 rows, the out-, gate|up and down-projections add
+ * each CTA's partial sums into 64-bit fixed-point accumulators (2^-30 units) with one atomic add per row, and the
+ * next projection's prologue reads the sums (the residual add, or silu(g) * u). Integer addition makes the result
+ * independent of the order of the adds. This flag turns that off: split 128-row tiles are finished instead by the
+ * last of their CTAs (an atomic ticket, the parts added in CTA order), as with more rows or ranks. On B200 at one
+ * rank and one row the accumulators measured 6.80 ms per step against 7.46 ms with tile finishing. */
+#define QRES_FLAG_TILE_FINISH 4
 
 /* one FP8-e4m3 projection, block-scaled (one fp32 scale per 128 x 128 block of the canonical matrix), in the
  * GEMV layout made by qres_tile_weight: rows in tiles of 128 (zero-padded), a tile's K in 128-wide units of
- * 16 KB stored back to back, inside a unit the tensor core's no-swizzle K-major core matrices (byte (r, c) at
- * (r / 8) * 1024 + (c / 16) * 128 + (r % 8) * 16 + c % 16). uscale points at the scale table: per tile, 128
+ * 16 KB stored back to back, inside a unit the tensor core's 128-byte-swizzled K-major arrangement (byte (r, c)
+ * at r * 128 + ((c / 16) ^ (r % 8)) * 16 + c % 16). uscale points at the scale table: per tile, 128
  * bytes of row selectors (row r's canonical 128-row block is the tile's slot sel[r], 0..7), then for each
  * 128-K block the 8 slots' fp32 scales -- (128 + (K / 128) * 32) bytes per tile. */
 typedef struct {

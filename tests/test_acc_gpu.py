@@ -1,0 +1,60 @@
+"""The fixed-point accumulators of the one-rank step (EPI_ACC: each CTA's partial sums of the out-, gate|up and
+down-projections added as 64-bit integers in 2^-30 units; the next prologue forms the residual add or
+silu(g) * u from them) against the tile-finishing path (split tiles summed in CTA order by their last CTA) and
+the oracle.
+
+Integer addition is associative, so the accumulated step must be bit-identical from run to run however the
+CTAs' atomic adds interleave: eager and CUDA-graph replays of the same inputs agree bit for bit. The two paths
+round differently (one float rounding of the exact sum of 2^-30-rounded parts, against fp32 additions in CTA
+order), so against each other they agree to 5e-3 relative and both stay within test_model_gpu's 2e-2 of the
+oracle, over three consecutive steps of the G G G A x2 + lm_head schedule at 1 and 2 rows."""
+import pytest
+import torch
+
+from oracle import refgen, step
+from tt_qwen_resident_b200 import weights
+from tt_qwen_resident_b200.model import ResidentModel
+from test_model_gpu import rel, setup8  # noqa: F401
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("rows", [1, 2])
+def test_accumulators_match_tile_finish_and_oracle(cuda, setup8, rows):
+    w8, P = setup8
+    layers, interval, pos = 8, 4, 100
+    st = refgen.random_state(6, 2, pos, pos + 64, seed=1)
+    g = torch.Generator().manual_seed(11)
+    xs = [torch.randn(rows, 5120, generator=g).bfloat16().float() for _ in range(3)]
+    out = {}
+    for tile_finish in (False, True):
+        model = ResidentModel(weights.canonical_from_fp8(w8), layers, interval, batch=rows, max_pos=pos + 64,
+                              lm_head=True, tile_finish=tile_finish)
+        for run in ("eager", "graph", "graph2"):
+            for u in range(rows):
+                model.load_state(st, user=u)
+            if run == "graph":
+                model.capture_trace()
+            res = []
+            for k, x0 in enumerate(xs):
+                model.step(model.token_state(x0, [pos + k] * rows))
+                model.check()
+                res.append((model.x().clone(), model.logits().clone(), model.argmax()))
+            if run == "graph2":
+                model.release_trace()
+            out[(tile_finish, run)] = res
+        model.close()
+    for k in range(3):
+        xa, la, aa = out[(False, "eager")][k]
+        for run in ("graph", "graph2"):  # bit-reproducible whatever order the adds land in
+            xg, lg_, ag = out[(False, run)][k]
+            assert torch.equal(xa, xg) and torch.equal(la, lg_) and aa == ag, (k, run)
+        xt, lt, _ = out[(True, "eager")][k]
+        assert rel(xa, xt) < 5e-3 and rel(la, lt) < 5e-3, k
+    # the first step against the oracle, row 0
+    ref = refgen.clone_state(st)
+    x_ref, lg = step.torch_step(xs[0][0], P, ref, layers, interval, lm_head=True)
+    xa, la, _ = out[(False, "eager")][0]
+    xa, la = (xa[0], la[0]) if rows > 1 else (xa, la)
+    assert rel(xa, x_ref) < 2e-2
+    assert rel(la, step.logits_bf16(lg)) < 2e-2

@@ -16,6 +16,7 @@ QRES_HIST_SLOTS = 8
 QRES_KV_BLOCK = 64
 QRES_FLAG_VERIFY = 1
 QRES_FLAG_CHAIN = 2
+QRES_FLAG_TILE_FINISH = 4
 QRES_TOPK = 32
 W_GDN_IN, W_ATTN_IN, W_OUT, W_GATEUP, W_DOWN, W_HEAD = range(6)
 W_FC = 6  # the MTP draft layer fc

@@ -66,9 +66,13 @@ struct GemvParams {
     int nkw;                // K blocks in this CTA's activation window (the most any CTA needs)
     float* part;            // [grid][2][8][128]: a CTA's split first / last tile
     int* ticket;            // [tiles]
-    const uint8_t* next_w;  // the next projection of the step: the start of this CTA's range is pulled into L2
-    int next_units;
-    int next_prefetch;      // units per CTA
+    L2Heads next;           // the next projection of the step: the heads of its CTA runs are pulled into L2
+    const long long* racc;  // PRO_RMSNORM_ADD: fixed-point partial source [users][K] (instead of red), or null
+    const long long* gacc;  // PRO_SILU_ACC: fixed-point gate|up sums [users][ld_gacc]
+    int ld_gacc;
+    long long* acc_out;     // EPI_ACC: fixed-point target [users][ld_out]
+    long long* zero;        // zeroed by this launch after its dependency wait (16-byte multiple)
+    size_t zero_words;
     uint32_t* err;
 };
 
@@ -132,6 +136,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 
     pdl_wait();
     const int users = p.users;
+    if (p.zero != nullptr) {
+        // a fixed-point buffer of a later launch (its previous readers have completed before this launch's wait)
+        uint4* z = reinterpret_cast<uint4*>(p.zero);
+        for (size_t i = (size_t)blockIdx.x * kGemvThreads + tid; i < p.zero_words / 2; i += (size_t)G * kGemvThreads)
+            z[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
 
     // ---- prologue: the activations' hi / lo operand for the K blocks of this CTA's window. Columns of users
     // past B (B < 4) are never written: an MMA column depends on its own operand column only.
@@ -195,6 +205,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                     r.z += q.z;
                     r.w += q.w;
                 }
+            } else if (p.racc != nullptr) {
+                const longlong2* a = reinterpret_cast<const longlong2*>(p.racc + (size_t)b * K + 4 * i);
+                const longlong2 a0 = __ldcg(a), a1 = __ldcg(a + 1);
+                r = make_float4(acc_decode(a0.x), acc_decode(a0.y), acc_decode(a1.x), acc_decode(a1.y));
             } else {
                 r = __ldcg(reinterpret_cast<const float4*>(p.red + (size_t)b * K) + i);
                 for (int s = 1; s < p.nsrc; ++s) {
@@ -215,7 +229,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     // rmsnorm with B <= 2 rows and K <= 8192 (the hidden size): one pass over x. Thread t's float4 j is
     // x[4 (t + 256 j) ..] -- K block warp + 8 j at lane -- so each warp writes the operand of the blocks it
     // holds, straight from registers.
-    constexpr bool kRegs = PRO != PRO_BF16 && B <= 2;
+    constexpr bool kRegs = (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) && B <= 2;
     constexpr int kXj = 8;
     const bool regs = kRegs && K <= kXj * 4 * kGemvThreads && p.seg == 0;
     float rn[B], rn2[B];  // rn2: the second segment's (two-segment prologue)
@@ -295,6 +309,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     const int npairs = regs ? 0 : B * nwin;
     for (int pr0 = warp; pr0 < npairs; pr0 += 32) {
         float hv[4][4];
+        // PRO_SILU_ACC: a lane's 4 columns 4 lane .. + 3 of K block kb are the gate|up rows 256 kb + 8 lane .. + 7:
+        // g(c), g(c+1), u(c), u(c+1), g(c+2), g(c+3), u(c+2), u(c+3) (quad-interleaved rows); all loads first
+        longlong2 gq[PRO == PRO_SILU_ACC ? 4 : 1][4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const int pr = pr0 + 8 * c;
@@ -302,6 +319,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             int kb = kb_start + ws;
             if (kb >= nkb) kb -= nkb;
             hv[c][0] = hv[c][1] = hv[c][2] = hv[c][3] = 0.f;
+            if (PRO == PRO_SILU_ACC) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) gq[PRO == PRO_SILU_ACC ? c : 0][j] = make_longlong2(0, 0);
+            }
             if (pr < npairs && b < users) {
                 if (PRO == PRO_BF16) {
                     const uint2 v = *reinterpret_cast<const uint2*>(p.in + (size_t)b * p.ld_in + kb * 128 + 4 * lane);
@@ -309,6 +330,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                     hv[c][1] = bf16hi(v.x);
                     hv[c][2] = bf16lo(v.y);
                     hv[c][3] = bf16hi(v.y);
+                } else if (PRO == PRO_SILU_ACC) {
+                    const longlong2* g = reinterpret_cast<const longlong2*>(p.gacc + (size_t)b * p.ld_gacc + (size_t)kb * 256 + 8 * lane);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) gq[PRO == PRO_SILU_ACC ? c : 0][j] = __ldcg(g + j);
                 } else {
                     const float4 v = xload(b, kb * 32 + lane);
                     hv[c][0] = v.x;
@@ -327,6 +352,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             if (PRO == PRO_BF16) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) h[j] = hv[c][j];
+            } else if (PRO == PRO_SILU_ACC) {
+                // h = bf16(silu(g) * u), the SwiGLU product the gate|up epilogue forms in the unfused path
+                const longlong2* q = gq[PRO == PRO_SILU_ACC ? c : 0];
+                const float g[4] = {acc_decode(q[0].x), acc_decode(q[0].y), acc_decode(q[2].x), acc_decode(q[2].y)};
+                const float u[4] = {acc_decode(q[1].x), acc_decode(q[1].y), acc_decode(q[3].x), acc_decode(q[3].y)};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) h[j] = __bfloat162float(__float2bfloat16_rn(silu_f(g[j]) * u[j]));
             } else {
                 // h = bf16(x * r), r of the block's segment
                 int kbq = kb_start + ws;
@@ -357,12 +389,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                 issue(i);
                 issued = i + 1;
             }
-            if (p.next_w != nullptr && p.next_prefetch > 0) {
-                const int nb = p.next_units / G, nr = p.next_units % G;
-                const int nu0 = blockIdx.x * nb + min((int)blockIdx.x, nr), ncnt = nb + ((int)blockIdx.x < nr ? 1 : 0);
-                const int pf = min(ncnt, p.next_prefetch);
-                if (pf > 0) l2_prefetch_share(p.next_w + (size_t)nu0 * kUnitBytes, (size_t)pf * kUnitBytes, 0, 1);
-            }
+            l2_prefetch_heads(p.next, blockIdx.x, G);
         }
     } else if (warp == 1) {
         // ---- MMA issuer
@@ -437,6 +464,16 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                         reinterpret_cast<float*>(p.out)[(size_t)b * p.ld_out + r] = v[b];
                     }
                 }
+            }
+        };
+        // EPI_ACC: this CTA's part of a tile's rows into the fixed-point accumulators (split or not alike)
+        auto red_tile = [&](int T, const float* v) {
+            const int r = T * kTileRows + row;
+            if (r < p.rows) {
+#pragma unroll
+                for (int b = 0; b < B; ++b)
+                    if (b < users)
+                        atomicAdd(reinterpret_cast<unsigned long long*>(p.acc_out + (size_t)b * p.ld_out + r), acc_encode(v[b]));
             }
         };
         // the tiles of this CTA split with other CTAs (only its first and its last tile can be), finished
@@ -528,7 +565,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             __syncwarp();
             if (lane == 0) mbar_arrive(&dempty[d]);
             if (Tc != cur) {
-                if (cur >= 0) {
+                if (cur >= 0 && EPI == EPI_ACC) {
+                    red_tile(cur, acc);
+                } else if (cur >= 0) {
                     // a tile that ends inside the range: the first one may be split (held for the end), any
                     // later one lies wholly in this CTA
                     if (cur == first_T && split_tile(cur)) {
@@ -546,13 +585,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = fmaf(v[2 * b] + v[2 * b + 1], s * ainv[wsc * 8 + b], acc[b]);
         }
-        if (cur >= 0 && !split_tile(cur)) {
-            store(cur, acc);
-            cur = -1;
+        if (EPI == EPI_ACC) {
+            if (cur >= 0) red_tile(cur, acc);
+        } else {
+            if (cur >= 0 && !split_tile(cur)) {
+                store(cur, acc);
+                cur = -1;
+            }
+            if (cur >= 0 && first_tile >= 0) finish_split(2, first_tile, first_acc, cur, acc);
+            else if (cur >= 0) finish_split(1, cur, acc, 0, acc);
+            else if (first_tile >= 0) finish_split(1, first_tile, first_acc, 0, first_acc);
         }
-        if (cur >= 0 && first_tile >= 0) finish_split(2, first_tile, first_acc, cur, acc);
-        else if (cur >= 0) finish_split(1, cur, acc, 0, acc);
-        else if (first_tile >= 0) finish_split(1, first_tile, first_acc, 0, first_acc);
     }
     if (warp == 0 && lane == 0) {
         // never release shared memory with a copy still landing in it
@@ -634,8 +677,7 @@ int gemv_grid(int users, int rows_pad, int K, int grid) {
 
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch,
-                        const GemvExchange* ex = nullptr) {
+                        void* work, size_t work_bytes, const L2Heads* next, const GemvExchange* ex = nullptr) {
     if (users < 1 || users > kMaxRows || w.K % 128 != 0 || w.rows_pad % kTileRows != 0 || w.rows_pad < w.rows ||
         w.rows_pad > kGemvMaxTiles * kTileRows)
         return cudaErrorInvalidValue;
@@ -652,14 +694,23 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.K = w.K;
     p.nkb = nkb;
     p.users = users;
-    p.x = pro != PRO_BF16 ? static_cast<const float*>(in) : nullptr;
+    p.x = (pro == PRO_RMSNORM || pro == PRO_RMSNORM_ADD) ? static_cast<const float*>(in) : nullptr;
     p.in = pro == PRO_BF16 ? static_cast<const uint16_t*>(in) : nullptr;
     p.ld_in = ld_in;
     p.red = red;
     p.x_out = x_out;
-    if (pro == PRO_RMSNORM_ADD && (red == nullptr || x_out == nullptr)) return cudaErrorInvalidValue;
     const GemvExchange none;
     const GemvExchange& e = ex ? *ex : none;
+    if (pro == PRO_RMSNORM_ADD && ((red == nullptr && e.racc == nullptr) || x_out == nullptr)) return cudaErrorInvalidValue;
+    if ((pro == PRO_SILU_ACC) != (e.gacc != nullptr) || (epi == EPI_ACC) != (e.acc_out != nullptr) || e.zero_words % 2 ||
+        (e.racc != nullptr && (pro != PRO_RMSNORM_ADD || e.nsrc != 1)))
+        return cudaErrorInvalidValue;
+    p.racc = e.racc;
+    p.gacc = e.gacc;
+    p.ld_gacc = e.ld_gacc;
+    p.acc_out = e.acc_out;
+    p.zero = e.zero;
+    p.zero_words = e.zero ? e.zero_words : 0;
     if (e.nsrc < 1 || e.nsrc > kMaxPeers || e.p2p_n < 0 || e.p2p_n > kMaxPeers) return cudaErrorInvalidValue;
     if ((epi == EPI_P2P) != (e.p2p_n > 0) || (e.tagged != nullptr && pro != PRO_RMSNORM_ADD) ||
         ((e.tagged != nullptr || e.p2p_n > 0) && e.epoch == nullptr))
@@ -680,9 +731,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.out = out;
     p.ld_out = ld_out;
     p.err = err;
-    p.next_w = next ? static_cast<const uint8_t*>(next->data) : nullptr;
-    p.next_units = next ? (next->rows_pad / kTileRows) * (next->K / 128) : 0;
-    p.next_prefetch = next ? next_prefetch : 0;
+    p.next = next ? *next : L2Heads{nullptr, 0, 0, 0, 0};
     uint8_t* wk = static_cast<uint8_t*>(work);
     p.ticket = reinterpret_cast<int*>(wk);
     p.part = reinterpret_cast<float*>(wk + (size_t)kGemvMaxTiles * 4);
@@ -705,6 +754,9 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     if (pro == PRO_BF16 && epi == EPI_F32) return launch_pe<PRO_BF16, EPI_F32>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_BF16) return launch_pe<PRO_BF16, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_P2P) return launch_pe<PRO_BF16, EPI_P2P>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_BF16 && epi == EPI_ACC) return launch_pe<PRO_BF16, EPI_ACC>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_RMSNORM_ADD && epi == EPI_ACC) return launch_pe<PRO_RMSNORM_ADD, EPI_ACC>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_SILU_ACC && epi == EPI_ACC) return launch_pe<PRO_SILU_ACC, EPI_ACC>(p, Bt, grid, smem, st, pdl);
     return cudaErrorInvalidValue;
 }
 

@@ -25,9 +25,9 @@
 namespace qres {
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
                         int ld_out, int grid, uint32_t* err, cudaStream_t st, bool pdl, const float* red, float* x_out,
-                        void* work, size_t work_bytes, const qres_weight* next, int next_prefetch,
-                        const GemvExchange* ex = nullptr);
+                        void* work, size_t work_bytes, const L2Heads* next, const GemvExchange* ex = nullptr);
 size_t gemv_workspace_bytes(int grid);
+int gemv_grid(int users, int rows_pad, int K, int grid);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -160,6 +160,7 @@ struct qres_ctx {
     void* gemv_work = nullptr;
     size_t gemv_work_bytes = 0;
     uint2 *xch = nullptr, *atag = nullptr;
+    long long* acc[3] = {};  // one rank: the out-, gate|up and down-projections' fixed-point sums (EPI_ACC)
     void* chain_work = nullptr;
     size_t chain_work_bytes = 0;
     ncclComm_t comm = nullptr;
@@ -207,7 +208,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // workspace layout: offsets of each scratch region
 struct Carve {
     size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, xch, atag, chain,
-        chain_bytes, total;
+        chain_bytes, acc[3], total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -239,6 +240,11 @@ Carve carve(const qres_ctx* c) {
     k.atag = take((size_t)R * c->ic * 8);
     k.chain_bytes = chain_workspace_bytes(2 * c->sm_count);
     k.chain = take(k.chain_bytes);
+    // fixed-point accumulators of the one-rank step: out-projection [rows][5120], gate|up [rows][2 x 17408],
+    // down-projection [rows][5120] (int64)
+    k.acc[0] = take((size_t)R * kHidden * 8);
+    k.acc[1] = take((size_t)R * 2 * c->ic * 8);
+    k.acc[2] = take((size_t)R * kHidden * 8);
     k.total = off;
     return k;
 }
@@ -276,7 +282,7 @@ qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qr
     if (cfg->rows < 1 || cfg->rows > QRES_MAX_ROWS || cfg->layers < 1)
         return fail(nullptr, QRES_ERR_ARG, "qres_create: rows %d, layers %d", cfg->rows, cfg->layers);
     if (cfg->vocab % nranks) return fail(nullptr, QRES_ERR_ARG, "qres_create: vocab %d not divisible by %d", cfg->vocab, nranks);
-    if (cfg->flags & ~(QRES_FLAG_VERIFY | QRES_FLAG_CHAIN))
+    if (cfg->flags & ~(QRES_FLAG_VERIFY | QRES_FLAG_CHAIN | QRES_FLAG_TILE_FINISH))
         return fail(nullptr, QRES_ERR_ARG, "qres_create: unknown flags %#x", cfg->flags);
     if ((cfg->flags & QRES_FLAG_VERIFY) && (cfg->rows < 2 || cfg->rows + 3 > QRES_HIST_SLOTS))
         return fail(nullptr, QRES_ERR_ARG, "qres_create: a verify step has 2..%d rows, not %d", QRES_HIST_SLOTS - 3,
@@ -436,6 +442,7 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->atag = reinterpret_cast<uint2*>(w + k.atag);
     c->chain_work = w + k.chain;
     c->chain_work_bytes = k.chain_bytes;
+    for (int i = 0; i < 3; ++i) c->acc[i] = reinterpret_cast<long long*>(w + k.acc[i]);
     return QRES_OK;
 }
 
@@ -572,19 +579,48 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         order.push_back(&L.w[QRES_W_DOWN]);
     }
     if (c->cfg.vocab) order.push_back(&c->head);
-    auto next_of = [&](const qres_weight* w) -> const qres_weight* {
+    // units k0 .. k0 + k - 1 of every CTA run of projection w as that launch will split it
+    auto heads_of = [&](const qres_weight& w, int k0, int k) -> L2Heads {
+        const int units = (w.rows_pad / 128) * (w.K / 128);
+        return L2Heads{static_cast<const uint8_t*>(w.data), units, gemv_grid(R, w.rows_pad, w.K, grid_of(w)), k0, k};
+    };
+    // (deeper prefetch, here or from the mixers, measured slower: it competes with the stream it precedes)
+    const int kPrefetchUnits = 2;  // 32 KB per CTA run
+    std::vector<L2Heads> next_heads(order.size());
+    for (size_t i = 0; i < order.size(); ++i) next_heads[i] = heads_of(*order[(i + 1) % order.size()], 0, kPrefetchUnits);
+    auto next_of = [&](const qres_weight* w) -> const L2Heads* {
         for (size_t i = 0; i < order.size(); ++i)
-            if (order[i] == w) return order[(i + 1) % order.size()];
+            if (order[i] == w) return &next_heads[i];
         return nullptr;
     };
-    const int kPrefetchUnits = 2;  // 32 KB per CTA
     auto gemv = [&](const qres_weight& w, int pro, const void* in, int ld_in, int epi, void* out, int ld_out,
                     const float* red, float* x_out, const char* what) -> qres_status {
         return K(gemv_launch(w, R, pro, in, ld_in, epi, out, ld_out, grid_of(w), c->err, st, true, red, x_out, c->gemv_work,
-                             c->gemv_work_bytes, next_of(&w), kPrefetchUnits),
+                             c->gemv_work_bytes, next_of(&w)),
                  what);
     };
+    // one rank: the out-, gate|up and down-projections accumulate into fixed-point buffers (EPI_ACC); the
+    // gate|up prologue adds the out-projection's sums to the residual, the down prologue forms silu(g) * u from
+    // gate|up's, the next rmsnorm prologue adds the down-projection's. Each launch zeroes the buffer of the
+    // launch after it (whose last reader, two launches back, has completed): down zeroes out's, out gate|up's,
+    // gate|up down's.
+    // (up to 2 rows: from 4 rows on, every CTA re-reading all rows' 64-bit sums costs more than the finish saves)
+    const bool accm = !tp && !chain && !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && R <= 2;
+    long long* const accA = c->acc[0];
+    long long* const accB = c->acc[1];
+    long long* const accC = c->acc[2];
+    const long long* pending_acc = nullptr;
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
+        if (pending_acc) {
+            GemvExchange ex;
+            ex.racc = pending_acc;
+            qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true, nullptr,
+                                          other, c->gemv_work, c->gemv_work_bytes, next_of(&w), &ex),
+                              what);
+            std::swap(cur, other);
+            pending_acc = nullptr;
+            return s;
+        }
         if (pending && p2p) {
             // the peer exchange xchg - 1: every rank's tagged partial, added in rank order
             const int j = xchg - 1, slot = j & 1;
@@ -596,7 +632,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             ex.tag_add = (uint32_t)j + 1u;
             qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true,
                                           reinterpret_cast<const float*>(ex.tagged), other, c->gemv_work,
-                                          c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
+                                          c->gemv_work_bytes, next_of(&w), &ex),
                               what);
             std::swap(cur, other);
             pending = false;
@@ -624,7 +660,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             for (int r = 0; r < n; ++r)
                 ex.peer_data[r] = reinterpret_cast<uint2*>(c->p2p_peer[r] + pl.data) + ((size_t)slot * 8 + c->rank) * R * kHidden;
             qres_status s = K(gemv_launch(w, R, 1, in, w.K, 4, nullptr, kHidden, grid_of(w), c->err, st, true, nullptr,
-                                          nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&w), kPrefetchUnits, &ex),
+                                          nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&w), &ex),
                               what);
             ++xchg;
             pending = true;
@@ -645,7 +681,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         ex.seg = kHidden;
         ex.seg2 = c->io.h_in;
         STEP(gemv_launch(c->fc, R, 0, c->xe, kHidden, 3, cur, kHidden, grid_of(c->fc), c->err, st, true, nullptr, nullptr,
-                         c->gemv_work, c->gemv_work_bytes, nullptr, 0, &ex),
+                         c->gemv_work, c->gemv_work_bytes, nullptr, &ex),
              "fc");
     }
     for (int l = 0; l < c->cfg.layers; ++l) {
@@ -733,6 +769,38 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             pn.ld_out = last ? c->vocab_local : c->ld_y;
             STEP(chain_launch(cp, 2 * c->sm_count, c->sm_count, c->chain_work, c->chain_work_bytes, st, true), "chain");
             std::swap(cur, other);
+            continue;
+        }
+        if (accm) {
+            const qres_weight& wo = L.w[QRES_W_OUT];
+            const qres_weight& wg = L.w[QRES_W_GATEUP];
+            const qres_weight& wd = L.w[QRES_W_DOWN];
+            GemvExchange eo;
+            eo.acc_out = accA;
+            eo.zero = accB;
+            eo.zero_words = (size_t)R * 2 * c->ic;
+            STEP(gemv_launch(wo, R, 1, c->o, wo.K, 5, nullptr, kHidden, grid_of(wo), c->err, st, true, nullptr, nullptr,
+                             c->gemv_work, c->gemv_work_bytes, next_of(&wo), &eo),
+                 "out-proj");
+            GemvExchange eg;
+            eg.racc = accA;
+            eg.acc_out = accB;
+            eg.zero = accC;
+            eg.zero_words = (size_t)R * kHidden;
+            STEP(gemv_launch(wg, R, 2, cur, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true, nullptr, other,
+                             c->gemv_work, c->gemv_work_bytes, next_of(&wg), &eg),
+                 "gate-up");
+            std::swap(cur, other);
+            GemvExchange ed;
+            ed.gacc = accB;
+            ed.ld_gacc = 2 * c->ic;
+            ed.acc_out = accC;
+            ed.zero = accA;
+            ed.zero_words = (size_t)R * kHidden;
+            STEP(gemv_launch(wd, R, 3, nullptr, wd.K, 5, nullptr, kHidden, grid_of(wd), c->err, st, true, nullptr, nullptr,
+                             c->gemv_work, c->gemv_work_bytes, next_of(&wd), &ed),
+                 "down");
+            pending_acc = accC;
             continue;
         }
         s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");
@@ -869,7 +937,7 @@ qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const voi
     }
     const int ld_out = epi == 1 ? w->rows / 2 : w->rows;
     cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, epi, out, ld_out, grid, err, static_cast<cudaStream_t>(stream),
-                                 false, nullptr, nullptr, work, work_bytes, nullptr, 0);
+                                 false, nullptr, nullptr, work, work_bytes, nullptr);
     if (ce != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(ce));
     return QRES_OK;
 }

@@ -138,6 +138,16 @@ struct GemvExchange {
     // normalised on its own; seg 0 = one segment
     const float* seg2 = nullptr;
     int seg = 0;
+    // fixed-point accumulators (one rank): the prologue's partial source (PRO_RMSNORM_ADD, int64 [users][K])
+    // instead of fp32 `red`; the SwiGLU prologue's gate|up sums (PRO_SILU_ACC, int64 [users][ld_gacc], rows in the
+    // interleaved quads of the gate|up matrix); the epilogue's target (EPI_ACC, int64 [users][ld_out]); and a
+    // buffer this launch zeroes after its dependency wait (the one a later launch accumulates into)
+    const long long* racc = nullptr;
+    const long long* gacc = nullptr;
+    int ld_gacc = 0;
+    long long* acc_out = nullptr;
+    long long* zero = nullptr;
+    size_t zero_words = 0;
 };
 
 // destinations of a small per-step peer exchange, double-buffered by step parity: this rank's region in each
@@ -222,6 +232,26 @@ __device__ __forceinline__ void l2_prefetch_share(const uint8_t* p, size_t bytes
 // L2 prefetch of a global range (no shared destination)
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// The heads of a weight-streaming projection's CTA runs: its `units` 16 KB units are split over `grid` CTAs in
+// contiguous runs (the first units % grid runs one longer), and units k0 .. k0 + k - 1 of every run are pulled
+// into L2, so that every CTA of that launch starts on L2 hits rather than only the first few.
+struct L2Heads {
+    const uint8_t* w;
+    int units, grid, k0, k;
+};
+
+// prefetcher i of n takes the runs i, i + n, ...
+__device__ __forceinline__ void l2_prefetch_heads(const L2Heads& h, int i, int n) {
+    if (h.w == nullptr || h.k <= 0 || h.grid <= 0) return;
+    const int base = h.units / h.grid, rem = h.units % h.grid;
+    for (int c = i; c < h.grid; c += n) {
+        const int u0 = c * base + min(c, rem), cnt = base + (c < rem ? 1 : 0);
+        const int m = min(cnt, h.k0 + h.k);
+        for (int u = h.k0; u < m; u += 4)
+            bulk_prefetch_l2(h.w + (size_t)(u0 + u) * 16384, (uint32_t)min(4, m - u) * 16384u);
+    }
 }
 
 // named barrier over a subset of warps (id 1.., count a multiple of 32)

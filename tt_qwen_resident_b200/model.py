@@ -57,6 +57,7 @@ class ResidentModel:
         verify=False,
         fc=None,
         chain=False,
+        tile_finish=False,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
@@ -86,7 +87,13 @@ class ResidentModel:
         L = _lib.lib()
         # chain: the projections between two mixers as one persistent launch (gemv_chain.cu) where the library
         # can (lm_head, <= 4 rows, peer exchange when nranks > 1); False (default): one launch per projection
-        flags = (_lib.QRES_FLAG_VERIFY if self.verify else 0) | (_lib.QRES_FLAG_CHAIN if chain else 0)
+        # tile_finish: split projection tiles finished by their last CTA (ticket) rather than summed in the
+        # fixed-point accumulators the library uses at one rank with up to 2 rows
+        flags = (
+            (_lib.QRES_FLAG_VERIFY if self.verify else 0)
+            | (_lib.QRES_FLAG_CHAIN if chain else 0)
+            | (_lib.QRES_FLAG_TILE_FINISH if tile_finish else 0)
+        )
         cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count, flags)
         h = ctypes.c_void_p()
         _lib.check(L.qres_create(ctypes.byref(cfg), rank, nranks, ctypes.byref(h)), None, "qres_create")
