@@ -6,8 +6,9 @@ the oracle.
 Integer addition is associative, so the accumulated step must be bit-identical from run to run however the
 CTAs' atomic adds interleave: eager and CUDA-graph replays of the same inputs agree bit for bit. The two paths
 round differently (one float rounding of the exact sum of 2^-30-rounded parts, against fp32 additions in CTA
-order), so against each other they agree to 5e-3 relative and both stay within test_model_gpu's 2e-2 of the
-oracle, over three consecutive steps of the G G G A x2 + lm_head schedule at 1 and 2 rows."""
+order); a flipped bf16 rounding of an activation carries on through the recurrent state, so by the third step
+the two agree to ~5e-3 relative (asserted: 1e-2), and each stays within test_model_gpu's 2e-2 of the oracle at
+every one of three consecutive steps of the G G G A x2 + lm_head schedule, at 1 and 2 rows."""
 import pytest
 import torch
 
@@ -44,17 +45,18 @@ def test_accumulators_match_tile_finish_and_oracle(cuda, setup8, rows):
                 model.release_trace()
             out[(tile_finish, run)] = res
         model.close()
+    # the oracle over the same three steps (row 0), both paths
+    ref = refgen.clone_state(st)
+    for k in range(3):
+        x_ref, lg = step.torch_step(xs[k][0], P, ref, layers, interval, lm_head=True)
+        for tf in (False, True):
+            xk, lk, _ = out[(tf, "eager")][k]
+            xk, lk = (xk[0], lk[0]) if rows > 1 else (xk, lk)
+            assert rel(xk, x_ref) < 2e-2 and rel(lk, step.logits_bf16(lg)) < 2e-2, (k, tf)
     for k in range(3):
         xa, la, aa = out[(False, "eager")][k]
         for run in ("graph", "graph2"):  # bit-reproducible whatever order the adds land in
             xg, lg_, ag = out[(False, run)][k]
             assert torch.equal(xa, xg) and torch.equal(la, lg_) and aa == ag, (k, run)
         xt, lt, _ = out[(True, "eager")][k]
-        assert rel(xa, xt) < 5e-3 and rel(la, lt) < 5e-3, k
-    # the first step against the oracle, row 0
-    ref = refgen.clone_state(st)
-    x_ref, lg = step.torch_step(xs[0][0], P, ref, layers, interval, lm_head=True)
-    xa, la, _ = out[(False, "eager")][0]
-    xa, la = (xa[0], la[0]) if rows > 1 else (xa, la)
-    assert rel(xa, x_ref) < 2e-2
-    assert rel(la, step.logits_bf16(lg)) < 2e-2
+        assert rel(xa, xt) < 1e-2 and rel(la, lt) < 1e-2, k

@@ -31,6 +31,7 @@ struct AttnParams {
     int h, nkv, G;            // local query heads, local KV heads, heads per KV head
     int ld_y;
     const uint16_t* y;        // [B][ld_y]: q (h*256) | gate (h*256) | k (nkv*256) | v (nkv*256)
+    const long long* yacc;    // or the in-projection's fixed-point sums, same layout (y null)
     const int32_t* pos;
     const int32_t* page_table;
     int max_pages, num_pages;
@@ -56,7 +57,7 @@ __host__ __device__ inline size_t attn_smem_bytes() {
     return 2 * 2 * (size_t)kPageBytes /* K,V double buffer */ + 64 /* barriers */;
 }
 
-__device__ __forceinline__ void rms_rope_head(const uint16_t* src, const float* w, const float* cs, const float* sn,
+__device__ __forceinline__ void rms_rope_head(const YIn src, const float* w, const float* cs, const float* sn,
                                               float* dst, float* red, bool round_bf16) {
     // one head of 256 dims by 256 threads: dst = rope(rmsnorm(src) * w) (optionally rounded to bf16)
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
@@ -86,7 +87,7 @@ __device__ __forceinline__ void rms_rope_head(const uint16_t* src, const float* 
 
 // the G query heads of a group at once (256 threads, one dim each): dst[j] = rope(rmsnorm(src_j) * w), fp32; all
 // loads in flight together and one reduction round for every head
-__device__ __forceinline__ void rms_rope_group(const uint16_t* src, int G, const float* w, const float* cs,
+__device__ __forceinline__ void rms_rope_group(const YIn src, int G, const float* w, const float* cs,
                                                const float* sn, float (*dst)[kHD], float (*red)[kMaxGroup]) {
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
     float v[kMaxGroup];
@@ -171,7 +172,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     const int nce = (npg + ppc - 1) / ppc;
     if (c >= nce) return;
     const int* pt = p.page_table + (size_t)(p.verify ? 0 : b) * p.max_pages;
-    const uint16_t* y = p.y + (size_t)b * p.ld_y;
+    const YIn yall{p.y, p.yacc};
+    const YIn y = yall.at((size_t)b * p.ld_y);
     const float* cs = p.cos_tab + (size_t)pos * (kRot / 2);
     const float* sn = p.sin_tab + (size_t)pos * (kRot / 2);
     const size_t head_stride = (size_t)kKvBlock * kHD;  // elements per (page, head)
@@ -201,15 +203,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnPar
     // q of the group's heads (fp32), all heads in one pass
     {
         __shared__ float redg[8][kMaxGroup];
-        rms_rope_group(y + (size_t)(g * G) * kHD, G, p.wq, cs, sn, qf, redg);
+        rms_rope_group(y.at((size_t)(g * G) * kHD), G, p.wq, cs, sn, qf, redg);
     }
     // k / v of the new positions p0 .. pos whose pages this CTA covers (row j's from its own y row)
     const int kbase = 2 * p.h * kHD;
     const int pg_lo = pg0 * kKvBlock, pg_hi = pg1 * kKvBlock;  // positions of this CTA's pages
     for (int t = max(p0, pg_lo); t <= pos && t < pg_hi; ++t) {
         const int j = t - p0;
-        const uint16_t* yj = p.y + (size_t)(p.verify ? j : b) * p.ld_y;
-        rms_rope_head(yj + kbase + (size_t)g * kHD, p.wk, p.cos_tab + (size_t)t * (kRot / 2),
+        const YIn yj = yall.at((size_t)(p.verify ? j : b) * p.ld_y);
+        rms_rope_head(yj.at(kbase + (size_t)g * kHD), p.wk, p.cos_tab + (size_t)t * (kRot / 2),
                       p.sin_tab + (size_t)t * (kRot / 2), knew[j], red, true);
         vnew[j][tid] = __uint_as_float((uint32_t)yj[kbase + p.nkv * kHD + g * kHD + tid] << 16);
     }
@@ -406,7 +408,7 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
                         void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
-                        const void* pf, size_t pf_bytes, int verify) {
+                        const void* pf, size_t pf_bytes, int verify, const long long* yacc) {
     if (nranks < 1 || 24 % nranks || rows < 1 || rows > kMaxRows || (verify && verify != rows)) return cudaErrorInvalidValue;
     if (work_bytes < attn_workspace_bytes(nranks, rows, nchunks)) return cudaErrorInvalidValue;
     AttnParams p;
@@ -414,7 +416,8 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
     p.nkv = nranks <= 4 ? 4 / nranks : 1;
     p.G = p.h / p.nkv;
     p.ld_y = ld_y;
-    p.y = y;
+    p.y = yacc ? nullptr : y;
+    p.yacc = yacc;
     p.pos = pos;
     p.page_table = page_table;
     p.max_pages = max_pages;

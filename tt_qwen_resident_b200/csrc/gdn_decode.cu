@@ -42,6 +42,7 @@ struct GdnParams {
     int nk, nv;              // local key / value heads
     int ld_y;                // elements between users' y rows
     const uint16_t* y;       // [B][ld_y] bf16: q | k | v | z | a | b
+    const long long* yacc;   // or the in-projection's fixed-point sums, same layout (y null)
     const int32_t* pos;      // [B]
     const uint16_t* taps;    // [conv][4] bf16
     const float* dt;         // [nv]
@@ -127,7 +128,8 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
     for (int row = 0; row < nrows; ++row) {
         const int bb = R ? row : b;  // the row's index in y / o
         const int pos = p0 + (R ? row : 0);
-        const uint16_t* y = p.y + (size_t)bb * p.ld_y;
+        const YIn yall{p.y, p.yacc};
+        const YIn y = yall.at((size_t)bb * p.ld_y);
         float* S = p.state + (R ? (size_t)((s0slot + row) % R) * slot_stride : (size_t)b * slot_stride) +
                    (size_t)hh * kDK * kDV + c0;
         if (!bad) {
@@ -151,7 +153,7 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
 #pragma unroll
                     for (int jj = 0; jj < 3; ++jj) {
                         const int q = pos - 3 + jj;
-                        hw[it][jj] = q >= p0 && R ? p.y[(size_t)(q - p0) * p.ld_y + ch]
+                        hw[it][jj] = q >= p0 && R ? yall[(size_t)(q - p0) * p.ld_y + ch]
                                                   : hist[(size_t)((q + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv + ch];
                     }
                     tp[it] = *reinterpret_cast<const uint2*>(p.taps + (size_t)ch * 4);
@@ -287,14 +289,15 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
-                       const void* pf, size_t pf_bytes, int verify, const int32_t* slot0) {
+                       const void* pf, size_t pf_bytes, int verify, const int32_t* slot0, const long long* yacc) {
     if (nranks < 1 || 16 % nranks || rows < 1 || rows > kMaxRows) return cudaErrorInvalidValue;
     if (verify && (verify != rows || rows + 3 > QRES_HIST_SLOTS || slot0 == nullptr)) return cudaErrorInvalidValue;
     GdnParams p;
     p.nk = 16 / nranks;
     p.nv = 48 / nranks;
     p.ld_y = ld_y;
-    p.y = y;
+    p.y = yacc ? nullptr : y;
+    p.yacc = yacc;
     p.pos = pos;
     p.taps = taps;
     p.dt = dt;

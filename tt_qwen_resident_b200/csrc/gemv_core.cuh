@@ -12,17 +12,6 @@ namespace qres {
 enum { PRO_RMSNORM = 0, PRO_BF16 = 1, PRO_RMSNORM_ADD = 2, PRO_SILU_ACC = 3 };
 enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3, EPI_P2P = 4, EPI_ACC = 5 };
 
-// Fixed-point accumulators (EPI_ACC): every CTA adds its fp32 partial of a row, rounded to a multiple of 2^-30,
-// into a 64-bit integer with one atomic add. Integer addition is associative, so the sum does not depend on the
-// order in which the CTAs' additions land (bit-reproducible without a ticket or a designated finisher); the
-// consumer (the next launch) reads it back as one float rounding of the exact sum of the rounded partials.
-// Range: |partial|, |sum| < 2^33.
-constexpr float kAccScale = 1073741824.0f;    // 2^30
-constexpr float kAccInv = 9.313225746154785e-10f;  // 2^-30
-__device__ __forceinline__ unsigned long long acc_encode(float v) {
-    return (unsigned long long)__float2ll_rn(v * kAccScale);
-}
-__device__ __forceinline__ float acc_decode(long long w) { return __ll2float_rn(w) * kAccInv; }
 constexpr int kMaxPeers = 8;
 
 constexpr int kGemvThreads = 256;

@@ -748,6 +748,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     if (pro == PRO_RMSNORM && epi == EPI_BF16) return launch_pe<PRO_RMSNORM, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_SILU_MUL) return launch_pe<PRO_RMSNORM, EPI_SILU_MUL>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_F32) return launch_pe<PRO_RMSNORM, EPI_F32>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_RMSNORM && epi == EPI_ACC) return launch_pe<PRO_RMSNORM, EPI_ACC>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_BF16) return launch_pe<PRO_RMSNORM_ADD, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_SILU_MUL) return launch_pe<PRO_RMSNORM_ADD, EPI_SILU_MUL>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_BF16 && epi == EPI_RESID) return launch_pe<PRO_BF16, EPI_RESID>(p, Bt, grid, smem, st, pdl);

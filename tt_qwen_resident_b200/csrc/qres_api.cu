@@ -31,14 +31,15 @@ int gemv_grid(int users, int rows_pad, int K, int grid);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
-                       const void* pf, size_t pf_bytes, int verify = 0, const int32_t* slot0 = nullptr);
+                       const void* pf, size_t pf_bytes, int verify = 0, const int32_t* slot0 = nullptr,
+                       const long long* yacc = nullptr);
 size_t attn_workspace_bytes(int nranks, int rows, int nchunks);
 int attn_default_chunks(int nranks, int rows, int sm_count, int max_pages);
 cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const int32_t* page_table,
                         int max_pages, int num_pages, const float* wq, const float* wk, const float* cos_tab,
                         const float* sin_tab, int max_pos, uint16_t* kp, uint16_t* vp, uint16_t* o, uint16_t* mixer_copy,
                         void* work, size_t work_bytes, int nchunks, uint32_t* err, cudaStream_t st, bool pdl,
-                        const void* pf, size_t pf_bytes, int verify = 0);
+                        const void* pf, size_t pf_bytes, int verify = 0, const long long* yacc = nullptr);
 cudaError_t tile_weight_launch(const uint8_t* src, int rows, int K, uint8_t* dst, cudaStream_t st);
 cudaError_t quantize_fp8_launch(const float* w, int N, int K, uint8_t* q, float* scales, cudaStream_t st);
 int topk_default_blocks(int n);
@@ -160,7 +161,9 @@ struct qres_ctx {
     void* gemv_work = nullptr;
     size_t gemv_work_bytes = 0;
     uint2 *xch = nullptr, *atag = nullptr;
-    long long* acc[3] = {};  // one rank: the out-, gate|up and down-projections' fixed-point sums (EPI_ACC)
+    // one rank: the out-projection's, gate|up's and the down-projection's fixed-point sums (EPI_ACC), and the
+    // in-projection's (read by the mixers), which follows the out-projection's in memory
+    long long* acc[4] = {};
     void* chain_work = nullptr;
     size_t chain_work_bytes = 0;
     ncclComm_t comm = nullptr;
@@ -208,7 +211,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // workspace layout: offsets of each scratch region
 struct Carve {
     size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, xch, atag, chain,
-        chain_bytes, acc[3], total;
+        chain_bytes, acc[4], total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -240,9 +243,11 @@ Carve carve(const qres_ctx* c) {
     k.atag = take((size_t)R * c->ic * 8);
     k.chain_bytes = chain_workspace_bytes(2 * c->sm_count);
     k.chain = take(k.chain_bytes);
-    // fixed-point accumulators of the one-rank step: out-projection [rows][5120], gate|up [rows][2 x 17408],
-    // down-projection [rows][5120] (int64)
-    k.acc[0] = take((size_t)R * kHidden * 8);
+    // fixed-point accumulators of the one-rank step (int64): out-projection [rows][5120] and right behind it the
+    // in-projection [rows][ld_y] (one range for the launch that zeroes both), gate|up [rows][2 x 17408],
+    // down-projection [rows][5120]
+    k.acc[0] = take((size_t)R * kHidden * 8 + (size_t)R * c->ld_y * 8);
+    k.acc[3] = k.acc[0] + (size_t)R * kHidden * 8;
     k.acc[1] = take((size_t)R * 2 * c->ic * 8);
     k.acc[2] = take((size_t)R * kHidden * 8);
     k.total = off;
@@ -442,7 +447,7 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->atag = reinterpret_cast<uint2*>(w + k.atag);
     c->chain_work = w + k.chain;
     c->chain_work_bytes = k.chain_bytes;
-    for (int i = 0; i < 3; ++i) c->acc[i] = reinterpret_cast<long long*>(w + k.acc[i]);
+    for (int i = 0; i < 4; ++i) c->acc[i] = reinterpret_cast<long long*>(w + k.acc[i]);
     return QRES_OK;
 }
 
@@ -609,6 +614,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     long long* const accA = c->acc[0];
     long long* const accB = c->acc[1];
     long long* const accC = c->acc[2];
+    long long* const accD = c->acc[3];
     const long long* pending_acc = nullptr;
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
         if (pending_acc) {
@@ -689,7 +695,18 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         const bool at = is_attn(c, l);
         uint16_t* mcopy = (l == c->cfg.layers - 1) ? c->io.mixer_out : nullptr;
         qres_status s = QRES_OK;
-        if (!chain || l == 0) {  // chained: layers > 0 get theirs from the previous chain
+        if (accm) {
+            // into the in-projection's accumulators (the mixer rounds the sums to bf16 as it reads them)
+            const qres_weight& wi = L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN];
+            GemvExchange ei;
+            ei.racc = pending_acc;
+            ei.acc_out = accD;
+            STEP(gemv_launch(wi, R, pending_acc ? 2 : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
+                             nullptr, pending_acc ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
+                 "in-proj");
+            if (pending_acc) std::swap(cur, other);
+            pending_acc = nullptr;
+        } else if (!chain || l == 0) {  // chained: layers > 0 get theirs from the previous chain
             s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
             if (s) return s;
         }
@@ -699,11 +716,11 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (at) {
             STEP(attn_launch(n, R, c->y, c->ld_y, pos, c->io.page_table, c->cfg.max_pages, c->cfg.num_pages, L.wq, L.wk,
                              c->cos_tab, c->sin_tab, c->max_pos, L.st.k_pool, L.st.v_pool, c->o, mcopy, c->attn_work,
-                             c->attn_work_bytes, c->attn_chunks, c->err, st, true, pf, pf_bytes, verify),
+                             c->attn_work_bytes, c->attn_chunks, c->err, st, true, pf, pf_bytes, verify, accm ? accD : nullptr),
                  "attention");
         } else {
             STEP(gdn_launch(n, R, c->y, c->ld_y, pos, L.taps, L.dt, L.neg_a, L.norm_w, L.st.gdn_state, L.st.conv_hist,
-                            c->o, mcopy, c->err, st, true, pf, pf_bytes, verify, &c->io.tok->slot),
+                            c->o, mcopy, c->err, st, true, pf, pf_bytes, verify, &c->io.tok->slot, accm ? accD : nullptr),
                  "gdn");
         }
         if (chain) {
@@ -795,8 +812,8 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             ed.gacc = accB;
             ed.ld_gacc = 2 * c->ic;
             ed.acc_out = accC;
-            ed.zero = accA;
-            ed.zero_words = (size_t)R * kHidden;
+            ed.zero = accA;  // and the in-projection's, right behind it
+            ed.zero_words = (size_t)R * kHidden + (size_t)R * c->ld_y;
             STEP(gemv_launch(wd, R, 3, nullptr, wd.K, 5, nullptr, kHidden, grid_of(wd), c->err, st, true, nullptr, nullptr,
                              c->gemv_work, c->gemv_work_bytes, next_of(&wd), &ed),
                  "down");

@@ -68,6 +68,28 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Fixed-point accumulators (the GEMV's EPI_ACC): every CTA adds its fp32 partial of a row, rounded to a multiple of 2^-30,
+// into a 64-bit integer with one atomic add. Integer addition is associative, so the sum does not depend on the
+// order in which the CTAs' additions land (bit-reproducible without a ticket or a designated finisher); the
+// consumer (the next launch) reads it back as one float rounding of the exact sum of the rounded partials.
+// Range: |partial|, |sum| < 2^33.
+constexpr float kAccScale = 1073741824.0f;    // 2^30
+constexpr float kAccInv = 9.313225746154785e-10f;  // 2^-30
+__device__ __forceinline__ unsigned long long acc_encode(float v) {
+    return (unsigned long long)__float2ll_rn(v * kAccScale);
+}
+__device__ __forceinline__ float acc_decode(long long w) { return __ll2float_rn(w) * kAccInv; }
+
+// the in-projection's output as the mixers read it: bf16 values, or (one rank) its fixed-point sums rounded to bf16
+struct YIn {
+    const uint16_t* y;
+    const long long* acc;
+    __device__ __forceinline__ uint16_t operator[](size_t i) const {
+        return acc ? __bfloat16_as_ushort(__float2bfloat16_rn(acc_decode(acc[i]))) : y[i];
+    }
+    __device__ __forceinline__ YIn at(size_t off) const { return YIn{y ? y + off : nullptr, acc ? acc + off : nullptr}; }
+};
+
 // ---- programmatic dependent launch --------------------------------------------------------------------------
 // wait: every prerequisite grid has completed and its memory is visible; launch_dependents: allow the next
 // kernel in the stream to be scheduled (its pre-wait part -- weight prefetch -- overlaps this kernel's tail)
