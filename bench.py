@@ -348,8 +348,9 @@ def run_ours(args, rank, world, local):
                 "layers": layers,
                 "parallelism": f"tp{world}",
                 "projections": "chained between mixers (gemv_chain)" if args.chain else "per-projection launches",
-                "split_tiles": ("fixed-point accumulators" if world == 1 and batch <= 2 and not args.chain
-                                and not args.tile_finish else "finished by ticket"),
+                "split_tiles": ("fixed-point accumulators" + (" (counted exchange over NVLink)" if world > 1 else "")
+                                if batch <= 2 and not args.chain and not args.tile_finish
+                                and (world == 1 or args.exchange == "p2p") else "finished by ticket"),
                 "exchange": ("fused NVLink peer exchange in the GEMV epilogue" if args.exchange == "p2p" else "NCCL")
                 if world > 1 else None,
                 "l2": "inputs larger than L2 (25.6 GB of weights streamed per step)",

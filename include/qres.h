@@ -79,12 +79,15 @@ typedef struct {
  * nranks > 1, the peer exchange; otherwise the per-projection path runs. Off by default: on B200 at one rank it
  * measured 4% slower than the per-projection launches (7.83 vs 7.52 ms per step). */
 #define QRES_FLAG_CHAIN 2
-/* qres_config.flags: at one rank, with an lm_head and up to 2 rows, the in-, out-, gate|up and down-projections
- * add each CTA's partial sums into 64-bit fixed-point accumulators (2^-30 units) with one atomic add per row, and
- * the consumer reads the sums: the next prologue (the residual add, or silu(g) * u) or the mixer (rounding them
- * to bf16). Integer addition makes the result independent of the order of the adds. This flag turns that off:
- * split 128-row tiles are finished instead by the last of their CTAs (an atomic ticket, the parts added in CTA
- * order), as with more rows or ranks. On B200 at one rank and one row the accumulators measured 6.51 ms per step
+/* qres_config.flags: with an lm_head and up to 2 rows (one rank, or ranks with the peer window of qres_p2p_open
+ * and native peer atomics), the in-, out-, gate|up and down-projections add each CTA's partial sums into 64-bit
+ * fixed-point accumulators (2^-30 units) with one atomic add per row, and the consumer reads the sums: the next
+ * prologue (the residual add, or silu(g) * u) or the mixer (rounding them to bf16). The row-parallel out- and
+ * down-projections add counted words ((value << 8) + 1) into every rank's accumulator over NVLink, and the next
+ * prologue reads a word once it holds every rank's contributions. Integer addition makes the result independent
+ * of the order of the adds and identical on every rank. This flag turns that off: split 128-row tiles are
+ * finished instead by the last of their CTAs (an atomic ticket, the parts added in CTA order) and ranks exchange
+ * tagged words, as with more rows. On B200 at one rank and one row the accumulators measured 6.51 ms per step
  * against 7.39 ms with tile finishing. */
 #define QRES_FLAG_TILE_FINISH 4
 

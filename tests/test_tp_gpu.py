@@ -1,14 +1,18 @@
 """Tensor parallelism on 2 GPUs: each rank runs ResidentModel on its shard (heads, MLP columns, vocab); the out- and
-down-projection partials are summed across ranks and the lm_head's per-rank top-32 lists are merged. Two
+down-projection partials are summed across ranks and the lm_head's per-rank top-32 lists are merged. Three
 exchanges are compared:
 - NCCL (the baseline): the GEMV writes its fp32 partial, ncclAllReduce sums it, the next GEMV's prologue adds it;
-- the fused peer exchange (qres_p2p_*): the GEMV epilogue stores each finished tile into both ranks' windows over
-  NVLink and the next GEMV's prologue waits for both ranks' counters and adds the partials in rank order.
-At n = 2 both form p0 + p1 and add it to x, so the two modes must agree bit for bit over an eager step and three
-CUDA-graph replays (which also exercises the exchange counters across steps). The first step must match the
-oracle run at n = 2 from the same state (x and each rank's logits within 2e-2 relative, the greedy pick by the
-argmax rule over the gathered logits), and both ranks must hold the same x bit for bit. Skipped with fewer than
-2 GPUs.
+- the tagged peer exchange (qres_p2p_*, tile finishing): the GEMV epilogue stores each finished tile into both
+  ranks' windows over NVLink as tagged words and the next prologue adds the ranks' partials in rank order. At
+  n = 2 it forms p0 + p1 like NCCL, so the two must agree bit for bit over an eager step and three CUDA-graph
+  replays (which also exercises the exchange tags across steps);
+- the counted fixed-point exchange (the default with peer atomics): every CTA adds its partial, as a counted
+  64-bit word, into both ranks' accumulators; the next prologue reads each word once it holds every
+  contribution. Integer sums do not depend on the order the adds land in, so both ranks hold the same x bit for
+  bit; against NCCL (a different rounding) x agrees to 1e-2 relative at every step.
+Each mode's first step must match the oracle run at n = 2 from the same state (x and each rank's logits within
+2e-2 relative, the greedy pick by the argmax rule over the gathered logits), and both ranks must hold the same x
+bit for bit at every step. Skipped with fewer than 2 GPUs.
 """
 import os
 
@@ -36,10 +40,10 @@ def _rank(rank, world, port, w8, out):
     dev = torch.device("cuda", rank)
     st = refgen.random_state(3, 1, 70, 134, seed=1)
     x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
-    for mode in ("nccl", "p2p"):
+    for mode in ("nccl", "p2p", "acc"):
         model = ResidentModel(weights.canonical_from_fp8(w8, device=dev), 4, 4, batch=1, max_pos=134, lm_head=True,
                               rank=rank, nranks=world, nccl_id=obj[0] if mode == "nccl" else None,
-                              p2p=mode == "p2p", device=dev)
+                              p2p=mode != "nccl", device=dev, tile_finish=mode != "acc")
         model.load_state(st)
         res = []
         for k in range(STEPS):
@@ -72,7 +76,7 @@ def test_tp2_decode_step_matches_oracle_nccl_and_peer_exchange():
     x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
     x_ref, lg = step.torch_step(x0, P, st, 4, 4, lm_head=True)
     rel = lambda a, b: float((a - b).norm() / b.norm())
-    for mode in ("nccl", "p2p"):
+    for mode in ("nccl", "p2p", "acc"):
         x0_, l0, a0 = out[(0, mode)][0]
         x1_, l1, a1 = out[(1, mode)][0]
         assert rel(x0_, x_ref) < 2e-2, mode
@@ -84,5 +88,6 @@ def test_tp2_decode_step_matches_oracle_nccl_and_peer_exchange():
             xp, lp, ap = out[(r, "p2p")][k]
             assert torch.equal(xn, xp), (k, r)  # the fused exchange reproduces the NCCL sum bit for bit
             assert torch.equal(ln, lp) and an == ap, (k, r)
-        for mode in ("nccl", "p2p"):
+        for mode in ("nccl", "p2p", "acc"):
             assert torch.equal(out[(0, mode)][k][0], out[(1, mode)][k][0]), (k, mode)  # ranks agree
+        assert rel(out[(0, "acc")][k][0], out[(0, "nccl")][k][0]) < 1e-2, k

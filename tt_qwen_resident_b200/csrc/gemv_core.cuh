@@ -9,8 +9,10 @@
 
 namespace qres {
 
-enum { PRO_RMSNORM = 0, PRO_BF16 = 1, PRO_RMSNORM_ADD = 2, PRO_SILU_ACC = 3 };
-enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3, EPI_P2P = 4, EPI_ACC = 5 };
+// PRO_RMSNORM_XACC / EPI_XACC: the counted fixed-point exchange between ranks (their own instantiations, so the
+// one-rank kernels carry none of its code)
+enum { PRO_RMSNORM = 0, PRO_BF16 = 1, PRO_RMSNORM_ADD = 2, PRO_SILU_ACC = 3, PRO_RMSNORM_XACC = 4 };
+enum { EPI_BF16 = 0, EPI_SILU_MUL = 1, EPI_RESID = 2, EPI_F32 = 3, EPI_P2P = 4, EPI_ACC = 5, EPI_XACC = 6 };
 
 constexpr int kMaxPeers = 8;
 

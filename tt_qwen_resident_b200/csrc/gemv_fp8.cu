@@ -73,6 +73,13 @@ struct GemvParams {
     long long* acc_out;     // EPI_ACC: fixed-point target [users][ld_out]
     long long* zero;        // zeroed by this launch after its dependency wait (16-byte multiple)
     size_t zero_words;
+    bool zero_sys;          // ... and fenced at system scope (other GPUs add into it later)
+    // EPI_ACC, counted exchange: every rank's accumulator (xn > 0), else acc_out alone (plain)
+    long long* xdst[kMaxPeers];
+    int xn;
+    // PRO_RMSNORM_ADD over counted racc: rc_ranks x (CTAs of the producing launch over the row's tile)
+    // contributions per word; the producer split its units as base rc_base, remainder rc_rem, rc_nkb per tile
+    int rc_ranks, rc_base, rc_rem, rc_nkb;
     uint32_t* err;
 };
 
@@ -139,8 +146,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     if (p.zero != nullptr) {
         // a fixed-point buffer of a later launch (its previous readers have completed before this launch's wait)
         uint4* z = reinterpret_cast<uint4*>(p.zero);
-        for (size_t i = (size_t)blockIdx.x * kGemvThreads + tid; i < p.zero_words / 2; i += (size_t)G * kGemvThreads)
+        bool wrote = false;
+        for (size_t i = (size_t)blockIdx.x * kGemvThreads + tid; i < p.zero_words / 2; i += (size_t)G * kGemvThreads) {
             z[i] = make_uint4(0u, 0u, 0u, 0u);
+            wrote = true;
+        }
+        // other GPUs add into this buffer only after they have seen this launch's own adds (which follow the
+        // prologue's barrier): the zeros must be visible system-wide first
+        if (p.zero_sys && wrote) __threadfence_system();
     }
 
     // ---- prologue: the activations' hi / lo operand for the K blocks of this CTA's window. Columns of users
@@ -186,6 +199,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             __nanosleep(32);
         }
     };
+    constexpr bool kAdd = PRO == PRO_RMSNORM_ADD || PRO == PRO_RMSNORM_XACC;  // residual + partial sums
     auto xload = [&](int b, int i) -> float4 {
         if (PRO == PRO_RMSNORM && p.seg) {
             const int s4 = p.seg / 4;
@@ -193,7 +207,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                           : reinterpret_cast<const float4*>(p.x2 + (size_t)b * p.seg)[i - s4];
         }
         float4 v = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
-        if (PRO == PRO_RMSNORM_ADD) {
+        if (kAdd) {
             // the sources summed in rank order first (n = 2: the same sum NCCL forms), then added to x
             float4 r;
             if (p.tagged != nullptr) {
@@ -205,6 +219,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                     r.z += q.z;
                     r.w += q.w;
                 }
+            } else if (PRO == PRO_RMSNORM_XACC) {
+                // counted words, complete (the sweep below)
+                const longlong2* a = reinterpret_cast<const longlong2*>(p.racc + (size_t)b * K + 4 * i);
+                const longlong2 a0 = __ldcg(a), a1 = __ldcg(a + 1);
+                r = make_float4(acc_decode_cnt(a0.x), acc_decode_cnt(a0.y), acc_decode_cnt(a1.x), acc_decode_cnt(a1.y));
             } else if (p.racc != nullptr) {
                 const longlong2* a = reinterpret_cast<const longlong2*>(p.racc + (size_t)b * K + 4 * i);
                 const longlong2 a0 = __ldcg(a), a1 = __ldcg(a + 1);
@@ -226,14 +245,40 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         }
         return v;
     };
+    // counted exchange over ranks: other GPUs' adds land at their own pace, so the CTA sweeps the accumulator words
+    // (bounded) until every word holds rc_ranks x (the producer's CTAs over the word's tile) contributions; the
+    // loads above then read complete words
+    if (PRO == PRO_RMSNORM_XACC) {
+        const int n4 = users * (K / 4), nk = p.rc_nkb;
+        for (uint32_t it = 0;; ++it) {
+            bool mine = true;
+#pragma unroll 4
+            for (int idx = tid; idx < n4; idx += kGemvThreads) {
+                const int b = idx / (K / 4), i = idx - b * (K / 4);
+                const long long* a = p.racc + (size_t)b * K + 4 * i;
+                const uint4 v0 = ld_volatile128(a), v1 = ld_volatile128(a + 2);
+                const int T = (4 * i) / kTileRows;
+                const uint32_t want = (uint32_t)p.rc_ranks * (uint32_t)(cta_of_unit(T * nk + nk - 1, p.rc_base, p.rc_rem) -
+                                                                        cta_of_unit(T * nk, p.rc_base, p.rc_rem) + 1);
+                mine = mine && (v0.x & 255u) == want && (v0.z & 255u) == want && (v1.x & 255u) == want &&
+                       (v1.z & 255u) == want;
+            }
+            if (__syncthreads_and(mine)) break;
+            if (it >= kPeerSpinLimit / 64) {
+                if (tid == 0) atomicOr(p.err, kErrPeer | kErrTimeout);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
     // rmsnorm with B <= 2 rows and K <= 8192 (the hidden size): one pass over x. Thread t's float4 j is
     // x[4 (t + 256 j) ..] -- K block warp + 8 j at lane -- so each warp writes the operand of the blocks it
     // holds, straight from registers.
-    constexpr bool kRegs = (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) && B <= 2;
+    constexpr bool kRegs = (PRO == PRO_RMSNORM || kAdd) && B <= 2;
     constexpr int kXj = 8;
     const bool regs = kRegs && K <= kXj * 4 * kGemvThreads && p.seg == 0;
     float rn[B], rn2[B];  // rn2: the second segment's (two-segment prologue)
-    if (PRO == PRO_RMSNORM || PRO == PRO_RMSNORM_ADD) {
+    if (PRO == PRO_RMSNORM || kAdd) {
         float4 xr[kRegs ? B : 1][kXj];
 #pragma unroll
         for (int b = 0; b < B; ++b) {
@@ -246,7 +291,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                         if (i < K / 4) {
                             v = xload(b, i);
-                            if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
+                            if (kAdd && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
                         }
                         xr[kRegs ? b : 0][j] = v;
                         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -256,7 +301,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 #pragma unroll 5
                     for (int i = tid; i < K / 4; i += kGemvThreads) {
                         const float4 v = xload(b, i);
-                        if (PRO == PRO_RMSNORM_ADD && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
+                        if (kAdd && blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
                         const float q = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                         if (p.seg && 4 * i >= p.seg) ss2 += q;
                         else ss += q;
@@ -471,9 +516,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             const int r = T * kTileRows + row;
             if (r < p.rows) {
 #pragma unroll
-                for (int b = 0; b < B; ++b)
-                    if (b < users)
-                        atomicAdd(reinterpret_cast<unsigned long long*>(p.acc_out + (size_t)b * p.ld_out + r), acc_encode(v[b]));
+                for (int b = 0; b < B; ++b) {
+                    if (b >= users) break;
+                    const size_t off = (size_t)b * p.ld_out + r;
+                    if (EPI == EPI_XACC) {
+                        // the counted exchange: into every rank's accumulator (remote adds over NVLink)
+                        const unsigned long long e = acc_encode_cnt(v[b]);
+                        for (int d = 0; d < p.xn; ++d) atomicAdd(reinterpret_cast<unsigned long long*>(p.xdst[d] + off), e);
+                    } else {
+                        atomicAdd(reinterpret_cast<unsigned long long*>(p.acc_out + off), acc_encode(v[b]));
+                    }
+                }
             }
         };
         // the tiles of this CTA split with other CTAs (only its first and its last tile can be), finished
@@ -565,7 +618,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
             __syncwarp();
             if (lane == 0) mbar_arrive(&dempty[d]);
             if (Tc != cur) {
-                if (cur >= 0 && EPI == EPI_ACC) {
+                if (cur >= 0 && (EPI == EPI_ACC || EPI == EPI_XACC)) {
                     red_tile(cur, acc);
                 } else if (cur >= 0) {
                     // a tile that ends inside the range: the first one may be split (held for the end), any
@@ -585,7 +638,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[b] = fmaf(v[2 * b] + v[2 * b + 1], s * ainv[wsc * 8 + b], acc[b]);
         }
-        if (EPI == EPI_ACC) {
+        if (EPI == EPI_ACC || EPI == EPI_XACC) {
             if (cur >= 0) red_tile(cur, acc);
         } else {
             if (cur >= 0 && !split_tile(cur)) {
@@ -694,7 +747,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.K = w.K;
     p.nkb = nkb;
     p.users = users;
-    p.x = (pro == PRO_RMSNORM || pro == PRO_RMSNORM_ADD) ? static_cast<const float*>(in) : nullptr;
+    p.x = (pro == PRO_RMSNORM || pro == PRO_RMSNORM_ADD || pro == PRO_RMSNORM_XACC) ? static_cast<const float*>(in) : nullptr;
     p.in = pro == PRO_BF16 ? static_cast<const uint16_t*>(in) : nullptr;
     p.ld_in = ld_in;
     p.red = red;
@@ -702,8 +755,11 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     const GemvExchange none;
     const GemvExchange& e = ex ? *ex : none;
     if (pro == PRO_RMSNORM_ADD && ((red == nullptr && e.racc == nullptr) || x_out == nullptr)) return cudaErrorInvalidValue;
-    if ((pro == PRO_SILU_ACC) != (e.gacc != nullptr) || (epi == EPI_ACC) != (e.acc_out != nullptr) || e.zero_words % 2 ||
-        (e.racc != nullptr && (pro != PRO_RMSNORM_ADD || e.nsrc != 1)))
+    if ((pro == PRO_SILU_ACC) != (e.gacc != nullptr) || (epi == EPI_ACC) != (e.acc_out != nullptr) ||
+        (epi == EPI_XACC) != (e.xn > 0) || e.zero_words % 2 ||
+        (e.racc != nullptr && pro == PRO_RMSNORM_ADD && (e.nsrc != 1 || e.rc_ranks != 0)) ||
+        (e.racc != nullptr && pro != PRO_RMSNORM_ADD && pro != PRO_RMSNORM_XACC) ||
+        (pro == PRO_RMSNORM_XACC && (e.racc == nullptr || e.rc_ranks < 1 || x_out == nullptr)))
         return cudaErrorInvalidValue;
     p.racc = e.racc;
     p.gacc = e.gacc;
@@ -711,6 +767,18 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.acc_out = e.acc_out;
     p.zero = e.zero;
     p.zero_words = e.zero ? e.zero_words : 0;
+    p.zero_sys = e.zero_sys;
+    if (e.xn < 0 || e.xn > kMaxPeers) return cudaErrorInvalidValue;
+    p.xn = e.xn;
+    for (int i = 0; i < kMaxPeers; ++i) p.xdst[i] = e.xdst[i];
+    p.rc_ranks = e.rc_ranks;
+    p.rc_nkb = e.rc_nkb;
+    p.rc_base = p.rc_rem = 0;
+    if (e.rc_ranks > 0) {
+        if (e.racc == nullptr || e.rc_grid < 1 || e.rc_nkb < 1 || e.rc_units < e.rc_grid) return cudaErrorInvalidValue;
+        p.rc_base = e.rc_units / e.rc_grid;
+        p.rc_rem = e.rc_units % e.rc_grid;
+    }
     if (e.nsrc < 1 || e.nsrc > kMaxPeers || e.p2p_n < 0 || e.p2p_n > kMaxPeers) return cudaErrorInvalidValue;
     if ((epi == EPI_P2P) != (e.p2p_n > 0) || (e.tagged != nullptr && pro != PRO_RMSNORM_ADD) ||
         ((e.tagged != nullptr || e.p2p_n > 0) && e.epoch == nullptr))
@@ -758,6 +826,11 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     if (pro == PRO_BF16 && epi == EPI_ACC) return launch_pe<PRO_BF16, EPI_ACC>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_RMSNORM_ADD && epi == EPI_ACC) return launch_pe<PRO_RMSNORM_ADD, EPI_ACC>(p, Bt, grid, smem, st, pdl);
     if (pro == PRO_SILU_ACC && epi == EPI_ACC) return launch_pe<PRO_SILU_ACC, EPI_ACC>(p, Bt, grid, smem, st, pdl);
+    // the counted exchange between ranks
+    if (pro == PRO_BF16 && epi == EPI_XACC) return launch_pe<PRO_BF16, EPI_XACC>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_SILU_ACC && epi == EPI_XACC) return launch_pe<PRO_SILU_ACC, EPI_XACC>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_RMSNORM_XACC && epi == EPI_ACC) return launch_pe<PRO_RMSNORM_XACC, EPI_ACC>(p, Bt, grid, smem, st, pdl);
+    if (pro == PRO_RMSNORM_XACC && epi == EPI_BF16) return launch_pe<PRO_RMSNORM_XACC, EPI_BF16>(p, Bt, grid, smem, st, pdl);
     return cudaErrorInvalidValue;
 }
 

@@ -112,10 +112,13 @@ bool load_nccl(const char* libpath, std::string* why) {
 // s * 2L + j + 1 (L layers; never 0, so the zeroed window holds no valid word); step s's lists use slot s % 2 and
 // their counters only grow (the k-th use of a slot completes at k).
 struct P2PLayout {
-    size_t lcnt = 0, data = 256, lists = 0, total = 0;
+    size_t lcnt = 0, data = 256, lists = 0, xa = 0, xc = 0, total = 0;
     explicit P2PLayout(int rows) {
         lists = data + (size_t)3 * 8 * rows * kHidden * 8;
-        total = lists + (size_t)2 * 8 * rows * 2 * QRES_TOPK * 4;
+        // the counted accumulators of the out- and down-projection exchanges (every rank adds into them)
+        xa = lists + (size_t)2 * 8 * rows * 2 * QRES_TOPK * 4;
+        xc = xa + (size_t)rows * kHidden * 8;
+        total = xc + (size_t)rows * kHidden * 8;
     }
 };
 
@@ -171,6 +174,7 @@ struct qres_ctx {
     uint8_t* p2p_local = nullptr;
     uint8_t* p2p_peer[8] = {};
     bool p2p_on = false;
+    bool p2p_atomics = false;  // 64-bit atomic adds to the peers' windows (native over NVLink)
     uint32_t* epoch = nullptr;  // steps completed (workspace), advanced by the feed kernel
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -493,6 +497,18 @@ qres_status qres_p2p_open(qres_ctx* c, const void* handles) {
     }
     CU(c, cudaMemset(c->epoch, 0, 4));
     CU(c, cudaDeviceSynchronize());
+    // the counted exchange adds into the peers' windows with 64-bit atomics: only where every other visible GPU
+    // has native peer atomics with this one
+    int ndev = 0;
+    CU(c, cudaGetDeviceCount(&ndev));
+    bool atomics = ndev >= c->nranks;
+    for (int d = 0; d < ndev && atomics; ++d) {
+        if (d == c->device) continue;
+        int v = 0;
+        if (cudaDeviceGetP2PAttribute(&v, cudaDevP2PAttrNativeAtomicSupported, c->device, d) != cudaSuccess || !v)
+            atomics = false;
+    }
+    c->p2p_atomics = atomics;
     c->p2p_on = true;
     return QRES_OK;
 }
@@ -604,27 +620,57 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                              c->gemv_work_bytes, next_of(&w)),
                  what);
     };
-    // one rank: the out-, gate|up and down-projections accumulate into fixed-point buffers (EPI_ACC); the
-    // gate|up prologue adds the out-projection's sums to the residual, the down prologue forms silu(g) * u from
-    // gate|up's, the next rmsnorm prologue adds the down-projection's. Each launch zeroes the buffer of the
-    // launch after it (whose last reader, two launches back, has completed): down zeroes out's, out gate|up's,
-    // gate|up down's.
-    // (up to 2 rows: from 4 rows on, every CTA re-reading all rows' 64-bit sums costs more than the finish saves)
-    const bool accm = !tp && !chain && !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && R <= 2;
-    long long* const accA = c->acc[0];
+    // Fixed-point accumulators (EPI_ACC, up to 2 rows, with an lm_head; over ranks with the peer exchange and native
+    // peer atomics). The in-projection and gate|up add into this rank's buffers (accD, read by the mixer; accB,
+    // read by the down prologue as silu(g) * u). The row-parallel out- and down-projections add into XA and XC,
+    // which the next rmsnorm prologue adds to the residual. Each launch zeroes a buffer whose last reader finished
+    // before it started and whose next writer starts after it.
+    // - One rank: plain sums, read after the producing launch has completed. Out-proj zeroes accB, gate|up XC,
+    //   down XA and accD (one range).
+    // - n ranks (EPI_XACC / PRO_RMSNORM_XACC): the out- and down-projections add counted words into every rank's
+    //   XA / XC (in the peer window), and the next prologue reads them once each word holds all contributions.
+    //   In-proj zeroes accB, out-proj XC, gate|up accD, down XA -- the exchange buffers with a system-scope fence:
+    //   peers add into them only after this rank's next contributions, which follow the fence.
+    const bool accm = !chain && !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && R <= 2 &&
+                      (!tp || (p2p && c->p2p_atomics));
     long long* const accB = c->acc[1];
-    long long* const accC = c->acc[2];
     long long* const accD = c->acc[3];
-    const long long* pending_acc = nullptr;
+    long long* xa_at[8] = {};
+    long long* xc_at[8] = {};
+    for (int r = 0; r < n; ++r) {
+        xa_at[r] = tp ? reinterpret_cast<long long*>(c->p2p_peer[r] + pl.xa) : c->acc[0];
+        xc_at[r] = tp ? reinterpret_cast<long long*>(c->p2p_peer[r] + pl.xc) : c->acc[2];
+    }
+    long long* const XA = xa_at[c->rank];
+    long long* const XC = xc_at[c->rank];
+    struct Pending {
+        const long long* acc = nullptr;
+        int units = 0, grid = 0, nkb = 0;  // the producing launch's partition (its per-tile contribution count)
+    } pending_acc;
+    auto producer_of = [&](const qres_weight& w, const long long* acc) {
+        Pending q;
+        q.acc = acc;
+        q.nkb = w.K / 128;
+        q.units = (w.rows_pad / 128) * q.nkb;
+        q.grid = gemv_grid(R, w.rows_pad, w.K, grid_of(w));
+        return q;
+    };
+    auto take_pending = [&](GemvExchange& ex) {
+        ex.racc = pending_acc.acc;
+        ex.rc_ranks = tp ? n : 0;
+        ex.rc_units = pending_acc.units;
+        ex.rc_grid = pending_acc.grid;
+        ex.rc_nkb = pending_acc.nkb;
+        pending_acc = Pending();
+    };
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
-        if (pending_acc) {
+        if (pending_acc.acc) {
             GemvExchange ex;
-            ex.racc = pending_acc;
-            qres_status s = K(gemv_launch(w, R, 2, cur, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true, nullptr,
+            take_pending(ex);
+            qres_status s = K(gemv_launch(w, R, tp ? 4 : 2, cur, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true, nullptr,
                                           other, c->gemv_work, c->gemv_work_bytes, next_of(&w), &ex),
                               what);
             std::swap(cur, other);
-            pending_acc = nullptr;
             return s;
         }
         if (pending && p2p) {
@@ -699,13 +745,17 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             // into the in-projection's accumulators (the mixer rounds the sums to bf16 as it reads them)
             const qres_weight& wi = L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN];
             GemvExchange ei;
-            ei.racc = pending_acc;
+            const bool add = pending_acc.acc != nullptr;
+            if (add) take_pending(ei);
             ei.acc_out = accD;
-            STEP(gemv_launch(wi, R, pending_acc ? 2 : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
-                             nullptr, pending_acc ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
+            if (tp) {
+                ei.zero = accB;
+                ei.zero_words = (size_t)R * 2 * c->ic;
+            }
+            STEP(gemv_launch(wi, R, add ? (tp ? 4 : 2) : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
+                             nullptr, add ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
                  "in-proj");
-            if (pending_acc) std::swap(cur, other);
-            pending_acc = nullptr;
+            if (add) std::swap(cur, other);
         } else if (!chain || l == 0) {  // chained: layers > 0 get theirs from the previous chain
             s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
             if (s) return s;
@@ -793,31 +843,46 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             const qres_weight& wg = L.w[QRES_W_GATEUP];
             const qres_weight& wd = L.w[QRES_W_DOWN];
             GemvExchange eo;
-            eo.acc_out = accA;
-            eo.zero = accB;
-            eo.zero_words = (size_t)R * 2 * c->ic;
-            STEP(gemv_launch(wo, R, 1, c->o, wo.K, 5, nullptr, kHidden, grid_of(wo), c->err, st, true, nullptr, nullptr,
+            if (tp) {
+                eo.xn = n;
+                for (int r = 0; r < n; ++r) eo.xdst[r] = xa_at[r];
+                eo.zero = XC;
+                eo.zero_words = (size_t)R * kHidden;
+                eo.zero_sys = true;
+            } else {
+                eo.acc_out = XA;
+                eo.zero = accB;
+                eo.zero_words = (size_t)R * 2 * c->ic;
+            }
+            STEP(gemv_launch(wo, R, 1, c->o, wo.K, tp ? 6 : 5, nullptr, kHidden, grid_of(wo), c->err, st, true, nullptr, nullptr,
                              c->gemv_work, c->gemv_work_bytes, next_of(&wo), &eo),
                  "out-proj");
             GemvExchange eg;
-            eg.racc = accA;
+            pending_acc = producer_of(wo, XA);
+            take_pending(eg);
             eg.acc_out = accB;
-            eg.zero = accC;
-            eg.zero_words = (size_t)R * kHidden;
-            STEP(gemv_launch(wg, R, 2, cur, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true, nullptr, other,
+            eg.zero = tp ? accD : XC;
+            eg.zero_words = tp ? (size_t)R * c->ld_y : (size_t)R * kHidden;
+            STEP(gemv_launch(wg, R, tp ? 4 : 2, cur, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true, nullptr, other,
                              c->gemv_work, c->gemv_work_bytes, next_of(&wg), &eg),
                  "gate-up");
             std::swap(cur, other);
             GemvExchange ed;
             ed.gacc = accB;
             ed.ld_gacc = 2 * c->ic;
-            ed.acc_out = accC;
-            ed.zero = accA;  // and the in-projection's, right behind it
-            ed.zero_words = (size_t)R * kHidden + (size_t)R * c->ld_y;
-            STEP(gemv_launch(wd, R, 3, nullptr, wd.K, 5, nullptr, kHidden, grid_of(wd), c->err, st, true, nullptr, nullptr,
+            ed.zero = XA;  // one rank: and accD, right behind it
+            ed.zero_words = (size_t)R * kHidden + (tp ? 0 : (size_t)R * c->ld_y);
+            if (tp) {
+                ed.xn = n;
+                for (int r = 0; r < n; ++r) ed.xdst[r] = xc_at[r];
+                ed.zero_sys = true;
+            } else {
+                ed.acc_out = XC;
+            }
+            STEP(gemv_launch(wd, R, 3, nullptr, wd.K, tp ? 6 : 5, nullptr, kHidden, grid_of(wd), c->err, st, true, nullptr, nullptr,
                              c->gemv_work, c->gemv_work_bytes, next_of(&wd), &ed),
                  "down");
-            pending_acc = accC;
+            pending_acc = producer_of(wd, XC);
             continue;
         }
         s = row_parallel(L.w[QRES_W_OUT], c->o, "out-proj");

@@ -79,6 +79,13 @@ __device__ __forceinline__ unsigned long long acc_encode(float v) {
     return (unsigned long long)__float2ll_rn(v * kAccScale);
 }
 __device__ __forceinline__ float acc_decode(long long w) { return __ll2float_rn(w) * kAccInv; }
+// Counted form (the row-parallel exchange): each contribution adds (value << 8) + 1, so the low byte counts the
+// contributions that have landed and a consumer that knows how many to expect can read a word as soon as it is
+// complete, whoever added it and in whatever order. Range: |sum| < 2^25.
+__device__ __forceinline__ unsigned long long acc_encode_cnt(float v) {
+    return ((unsigned long long)__float2ll_rn(v * kAccScale) << 8) + 1ull;
+}
+__device__ __forceinline__ float acc_decode_cnt(long long w) { return __ll2float_rn(w >> 8) * kAccInv; }
 
 // the in-projection's output as the mixers read it: bf16 values, or (one rank) its fixed-point sums rounded to bf16
 struct YIn {
@@ -170,6 +177,14 @@ struct GemvExchange {
     long long* acc_out = nullptr;
     long long* zero = nullptr;
     size_t zero_words = 0;
+    bool zero_sys = false;  // the zeroed buffer receives other GPUs' adds later: fence the zeroing at system scope
+    // the counted row-parallel exchange (EPI_ACC with xn > 0): each partial goes, as a counted word, into every
+    // rank's accumulator xdst[0..xn-1] (the peers' mapped over NVLink; xn = 1: this rank's alone), and the next
+    // prologue reads its racc once every word holds rc_ranks x (the producing launch's CTAs over the row's tile)
+    // contributions -- the producing launch split rc_units units of rc_nkb per tile over rc_grid CTAs
+    long long* xdst[8] = {};
+    int xn = 0;
+    int rc_ranks = 0, rc_units = 0, rc_grid = 0, rc_nkb = 0;
 };
 
 // destinations of a small per-step peer exchange, double-buffered by step parity: this rank's region in each
