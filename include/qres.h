@@ -64,7 +64,7 @@ typedef struct {
     int32_t max_pages;     /* page-table entries per user */
     int32_t num_pages;     /* pages in each attention layer's K (and V) pool */
     int32_t sm_count;      /* SMs to use; 0 = the device's (the weight-streaming kernels run 2 CTAs per SM) */
-    int32_t flags;         /* QRES_FLAG_VERIFY | QRES_FLAG_CHAIN | QRES_FLAG_TILE_FINISH, or 0 */
+    int32_t flags;         /* QRES_FLAG_VERIFY | QRES_FLAG_TILE_FINISH, or 0 */
 } qres_config;
 
 /* qres_config.flags: the verify step (ResidentModel(verify=True), model.py:416-457): the `rows` rows (2..5) are
@@ -73,12 +73,6 @@ typedef struct {
  * continuing after accepting row k uses position p + k + 1 and slot (tok.slot + k) % rows (no rollback). The
  * conv history and the KV cache are position-keyed and need nothing. */
 #define QRES_FLAG_VERIFY 1
-/* qres_config.flags: run the projections between two mixers (out-proj, gate|up, down, next in-proj or lm_head)
- * as one persistent launch (gemv_chain.cu: the weight stream runs on across the projections, their data
- * dependencies go through tagged words) instead of one launch each. Needs an lm_head, at most 4 rows and, with
- * nranks > 1, the peer exchange; otherwise the per-projection path runs. Off by default: on B200 at one rank it
- * measured 4% slower than the per-projection launches (7.83 vs 7.52 ms per step). */
-#define QRES_FLAG_CHAIN 2
 /* qres_config.flags: with an lm_head and up to 2 rows (one rank, or ranks with the peer window of qres_p2p_open
  * and native peer atomics), the in-, out-, gate|up and down-projections add each CTA's partial sums into 64-bit
  * fixed-point accumulators (2^-30 units) with one atomic add per row, and the consumer reads the sums: the next
@@ -159,9 +153,34 @@ QRES_API qres_status qres_load_gdn_params(qres_ctx* ctx, int32_t layer, const ui
 QRES_API qres_status qres_load_attn_params(qres_ctx* ctx, int32_t layer, const float* wq, const float* wk);
 /* Per-layer decode state buffers (State, model.py:151-174; load_state :1447-1470 writes their contents). */
 QRES_API qres_status qres_bind_state(qres_ctx* ctx, int32_t layer, const qres_layer_state* st);
+/* Write user `user`'s decode state of GDN layer `layer` into the bound buffers (ResidentModel.load_state,
+ * model.py:1447-1470): `state` = this rank's heads' fp32 state [48/n][128][128]; `hist3` = the layer's conv inputs
+ * at positions pos-3 .. pos-1 (oldest first), bf16 [3][conv_ch/n], stored into their history-ring slots (position
+ * p in slot p % QRES_HIST_SLOTS); hist3 may be NULL. Device pointers, copied on `stream`. A verify context takes
+ * `user` as the state slot. Layers that share a state buffer share what is written. */
+QRES_API qres_status qres_load_gdn_state(qres_ctx* ctx, int32_t layer, int32_t user, const float* state,
+                                         const uint16_t* hist3, int32_t pos, void* stream);
+/* Read user `user`'s fp32 state [48/n][128][128] of GDN layer `layer` (the reference reads State back with its
+ * ttnn.to_torch of the state tensors, model.py:1447-1470). */
+QRES_API qres_status qres_dump_gdn_state(qres_ctx* ctx, int32_t layer, int32_t user, float* state, void* stream);
+/* Write user `user`'s K and V rows of attention layer `layer` for positions 0 .. npos-1 (bf16 [kv_heads_local]
+ * [npos][256] each, device pointers) into the pages its page table names (io.page_table; position p in page
+ * page_table[user][p / 64], row p % 64). Other positions' rows are untouched. A page index outside the pool sets
+ * the device error word (qres_check). */
+QRES_API qres_status qres_load_kv(qres_ctx* ctx, int32_t layer, int32_t user, const uint16_t* k, const uint16_t* v,
+                                  int32_t npos, void* stream);
+/* Read positions 0 .. npos-1 of user `user`'s K and V rows of attention layer `layer` back, same layout. */
+QRES_API qres_status qres_dump_kv(qres_ctx* ctx, int32_t layer, int32_t user, uint16_t* k, uint16_t* v, int32_t npos,
+                                  void* stream);
 /* Rope tables [max_pos][32] fp32 cos and sin of model.py:128-131 (fp64 angles rounded to fp32). */
 QRES_API qres_status qres_bind_rope(qres_ctx* ctx, const float* cos_tab, const float* sin_tab, int32_t max_pos);
 QRES_API qres_status qres_bind_io(qres_ctx* ctx, const qres_io* io);
+/* The sampling parameters of the fed token (ResidentModel.set_sampling, model.py:1528-1551; the hub's draw,
+ * sampling.hpp:113-143 over the final top-32 list): `words` = device [rows][4] uint32 -- 1 / temperature in Q16
+ * (0 = greedy), top-k (<= 1 greedy, at most 32), top-p in Q16 (65536 = off), seed -- read by every step until
+ * bound again; NULL (the default) = greedy. The step then writes out[row] = {drawn token, position + 1, greedy
+ * argmax, 0} and, in feed mode, feeds the drawn token. The draw's random number hashes (seed, position). */
+QRES_API qres_status qres_bind_sampling(qres_ctx* ctx, const uint32_t* words);
 /* Scratch the step needs (activations, split-K partials, counters, the error word). */
 QRES_API qres_status qres_workspace_size(const qres_ctx* ctx, size_t* bytes);
 QRES_API qres_status qres_bind_workspace(qres_ctx* ctx, void* dev, size_t bytes);
@@ -189,6 +208,13 @@ QRES_API qres_status qres_p2p_alloc(qres_ctx* ctx, void* handle64);
  * the step to the peer exchange. Needs the workspace bound; resets the device step count the exchange counters
  * derive from, so every rank opens before any rank's first step (a barrier after the call). */
 QRES_API qres_status qres_p2p_open(qres_ctx* ctx, const void* handles);
+
+/* The exchange the step uses between ranks, as the context is configured now: QRES_XCHG_NONE (one rank),
+ * QRES_XCHG_NCCL (qres_nccl_init), QRES_XCHG_TAGGED (peer window, tagged words), QRES_XCHG_COUNTED (peer window,
+ * counted fixed-point words; needs native 64-bit peer atomics between every pair of ranks' GPUs, checked at
+ * qres_p2p_open where the process sees those GPUs -- otherwise the tagged exchange runs). Negative: bad context. */
+typedef enum { QRES_XCHG_NONE = 0, QRES_XCHG_NCCL = 1, QRES_XCHG_TAGGED = 2, QRES_XCHG_COUNTED = 3 } qres_exchange;
+QRES_API int32_t qres_exchange_mode(const qres_ctx* ctx);
 
 /* ---- the step (ResidentModel.step, model.py:1499-1508) ---- */
 /* Enqueue one decode step on `stream`. */
@@ -232,6 +258,12 @@ QRES_API qres_status qres_attn_mixer(int32_t nranks, int32_t rows, const uint16_
 QRES_API qres_status qres_topk_workspace_size(int32_t rows, int32_t n_logits, size_t* bytes);
 QRES_API qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, int32_t base, uint32_t* lists,
                       int32_t* argmax, void* work, size_t work_bytes, void* stream);
+
+/* The sampling draw alone (sampling.hpp:113-143): for each of `rows` rows, the token drawn from its top-32 list
+ * (lists [rows][64]: keys descending then indices, as qres_topk writes them) with its parameter words
+ * (words [rows][4], see qres_bind_sampling) at its position (pos [rows]) into token [rows]. Device pointers. */
+QRES_API qres_status qres_sample(int32_t rows, const uint32_t* lists, const uint32_t* words, const int32_t* pos,
+                                 int32_t* token, void* stream);
 
 /* The same top-32 / argmax as qres_topk without a workspace argument: it allocates nothing. It has no
  * counterpart in the reference. It is for callers that cannot allocate device memory -- a host framework that

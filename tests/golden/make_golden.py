@@ -9,7 +9,7 @@ are recorded, as are two single-kind schedules. The sampling fixture runs the in
 reference's ``tests/test_resident_sampling.py:37-95`` (loaded from its source text, the file's hardware fixture
 left out) on seeded logits for the five parameter cases of that test (:27-33).
 
-Usage:  python tests/golden/make_golden.py [REF_ROOT]   (default /root/reference)
+Usage:  python tests/golden/make_golden.py REF_ROOT   (or QRES_REFERENCE_ROOT=REF_ROOT in the environment)
 Writes: tests/golden/decode_steps.npz, gdn_steps.npz, attn_steps.npz, sampling.json
 """
 import ast
@@ -23,7 +23,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 SAMPLE_IDX = torch.randperm(48 * 128 * 128, generator=torch.Generator().manual_seed(3))[:8192]
-REF_ROOT = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF_ROOT = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QRES_REFERENCE_ROOT")
+if not REF_ROOT:
+    sys.exit("usage: make_golden.py REFERENCE_ROOT   (or set QRES_REFERENCE_ROOT): the sott0n/tt-qwen-resident checkout")
 
 
 def import_reference():

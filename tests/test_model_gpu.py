@@ -171,3 +171,41 @@ def test_layer_schedules_parity(cuda, setup8, layers, interval):
     o_ref = torch.cat([o for l, _, o in mix if l == layers - 1])
     errs = (rel(model.mixer_output(), o_ref), rel(model.x(), x_ref), rel(model.logits(), step.logits_bf16(lg)))
     assert max(errs) < 2e-2, errs
+
+
+def test_batch8_decode_steps_parity(cuda, setup8):
+    """BASELINE config 4's shape at 8 layers: 8 users per step, each with its own decode state (GDN states, conv
+    histories, KV cache behind a shuffled page table) at its own position, two consecutive steps carried on both
+    sides (model.py:421-446 users as rows, :780-823 per-user state). Every user's x, logits, greedy pick, GDN
+    states and appended KV row against its own oracle chain."""
+    w8, P = setup8
+    layers, interval, B, max_pos = 8, 4, 8, 384
+    pos = [40 + 37 * u for u in range(B)]
+    sts = [refgen.random_state(6, 2, pos[u], max_pos, seed=100 + u) for u in range(B)]
+    max_pages = max_pos // 64
+    pt = torch.randperm(B * max_pages, generator=torch.Generator().manual_seed(5)).to(torch.int32).view(B, max_pages)
+    model = ResidentModel(weights.canonical_from_fp8(w8), layers, interval, batch=B, max_pos=max_pos, lm_head=True,
+                          page_table=pt)
+    for u in range(B):
+        model.load_state(sts[u], user=u)
+    refs = [refgen.clone_state(s) for s in sts]
+    g = torch.Generator().manual_seed(21)
+    for k in range(2):
+        x0 = torch.randn(B, 5120, generator=g).bfloat16().float()
+        model.step(model.token_state(x0, [p + k for p in pos]))
+        model.check()
+        X, LG, AM = model.x(), model.logits(), model.argmax()
+        for u in range(B):
+            x_ref, lg = step.torch_step(x0[u], P, refs[u], layers, interval, lm_head=True)
+            lr = step.logits_bf16(lg)
+            assert rel(X[u], x_ref) < 2e-2, (k, u)
+            assert rel(LG[u], lr) < 2e-2, (k, u)
+            d, o = AM[u], sampling.argmax_rule(lr)
+            assert d == sampling.argmax_rule(LG[u]), (k, u)
+            if d != o:
+                assert float(lr[o] - lr[d]) <= float((LG[u][o] - lr[o]).abs() + (LG[u][d] - lr[d]).abs()), (k, u)
+    for u in range(B):
+        for c in range(6):
+            assert rel(model.gdn_state[c][u].cpu(), refs[u].gdn[c]) < 2e-2, (u, c)
+        k_dev = model.kv_rows(1, [pos[u], pos[u] + 1], user=u)
+        assert rel(k_dev, refs[u].K[1][:, pos[u] : pos[u] + 2]) < 2e-2, u

@@ -45,6 +45,7 @@ def _rank(rank, world, port, w8, out):
                               rank=rank, nranks=world, nccl_id=obj[0] if mode == "nccl" else None,
                               p2p=mode != "nccl", device=dev, tile_finish=mode != "acc")
         model.load_state(st)
+        out[(rank, mode, "exchange")] = model.exchange
         res = []
         for k in range(STEPS):
             if k == 1:
@@ -76,6 +77,10 @@ def test_tp2_decode_step_matches_oracle_nccl_and_peer_exchange():
     x0 = torch.randn(5120, generator=torch.Generator().manual_seed(3)).bfloat16().float()
     x_ref, lg = step.torch_step(x0, P, st, 4, 4, lm_head=True)
     rel = lambda a, b: float((a - b).norm() / b.norm())
+    # each mode ran the exchange it names (the counted one needs native peer atomics between the two GPUs)
+    for r in range(world):
+        assert out[(r, "nccl", "exchange")] == "nccl" and out[(r, "p2p", "exchange")] == "tagged"
+        assert out[(r, "acc", "exchange")] == "counted"
     for mode in ("nccl", "p2p", "acc"):
         x0_, l0, a0 = out[(0, mode)][0]
         x1_, l1, a1 = out[(1, mode)][0]

@@ -1,4 +1,4 @@
-"""ctypes binding of libqres.so (include/qres.h) and the torch custom ops over it.
+"""ctypes binding of libqres.so (include/qres.h); the torch custom ops over it are in ops.py.
 
 The library is built in-tree (``tt_qwen_resident_b200/libqres.so``, see ``build.py``). Nothing here falls back
 to another implementation: without the library (or a CUDA device) every entry point raises.
@@ -15,11 +15,11 @@ QRES_MAX_ROWS = 8
 QRES_HIST_SLOTS = 8
 QRES_KV_BLOCK = 64
 QRES_FLAG_VERIFY = 1
-QRES_FLAG_CHAIN = 2
 QRES_FLAG_TILE_FINISH = 4
 QRES_TOPK = 32
 W_GDN_IN, W_ATTN_IN, W_OUT, W_GATEUP, W_DOWN, W_HEAD = range(6)
 W_FC = 6  # the MTP draft layer fc
+XCHG_NAMES = {0: "none", 1: "nccl", 2: "tagged", 3: "counted"}  # qres_exchange_mode
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA error", 3: "device error", 4: "out of order", 5: "communication"}
 
 # the C-ABI entry points of include/qres.h (checked by tests/test_abi.py)
@@ -31,8 +31,13 @@ EXPORTS = [
     "qres_load_gdn_params",
     "qres_load_attn_params",
     "qres_bind_state",
+    "qres_load_gdn_state",
+    "qres_dump_gdn_state",
+    "qres_load_kv",
+    "qres_dump_kv",
     "qres_bind_rope",
     "qres_bind_io",
+    "qres_bind_sampling",
     "qres_workspace_size",
     "qres_bind_workspace",
     "qres_nccl_unique_id",
@@ -40,6 +45,7 @@ EXPORTS = [
     "qres_p2p_window_size",
     "qres_p2p_alloc",
     "qres_p2p_open",
+    "qres_exchange_mode",
     "qres_decode_step",
     "qres_capture",
     "qres_replay",
@@ -54,6 +60,7 @@ EXPORTS = [
     "qres_topk_workspace_size",
     "qres_topk",
     "qres_topk_noalloc",
+    "qres_sample",
     "qres_quantize_fp8",
     "qres_tile_weight",
 ]
@@ -133,8 +140,13 @@ def lib():
             "qres_load_gdn_params": [vp, i32, vp, vp, vp, vp],
             "qres_load_attn_params": [vp, i32, vp, vp],
             "qres_bind_state": [vp, i32, ctypes.POINTER(LayerState)],
+            "qres_load_gdn_state": [vp, i32, i32, vp, vp, i32, vp],
+            "qres_dump_gdn_state": [vp, i32, i32, vp, vp],
+            "qres_load_kv": [vp, i32, i32, vp, vp, i32, vp],
+            "qres_dump_kv": [vp, i32, i32, vp, vp, i32, vp],
             "qres_bind_rope": [vp, vp, vp, i32],
             "qres_bind_io": [vp, ctypes.POINTER(Io)],
+            "qres_bind_sampling": [vp, vp],
             "qres_workspace_size": [vp, ctypes.POINTER(sz)],
             "qres_bind_workspace": [vp, vp, sz],
             "qres_nccl_unique_id": [ctypes.c_char_p, vp],
@@ -155,6 +167,7 @@ def lib():
             "qres_topk_workspace_size": [i32, i32, ctypes.POINTER(sz)],
             "qres_topk": [i32, vp, i32, i32, vp, vp, vp, sz, vp],
             "qres_topk_noalloc": [i32, vp, i32, i32, vp, vp, vp],
+            "qres_sample": [i32, vp, vp, vp, vp, vp],
             "qres_quantize_fp8": [vp, i32, i32, vp, vp, vp],
             "qres_tile_weight": [vp, i32, i32, vp, vp],
         }
@@ -162,8 +175,9 @@ def lib():
             f = getattr(L, name)
             f.argtypes = args
             f.restype = ctypes.c_int
-        L.qres_step_launches.argtypes = [vp]
-        L.qres_step_launches.restype = ctypes.c_int32
+        for name in ("qres_step_launches", "qres_exchange_mode"):
+            getattr(L, name).argtypes = [vp]
+            getattr(L, name).restype = ctypes.c_int32
         _lib = L
     return _lib
 
@@ -251,17 +265,3 @@ def topk(logits, base=0, work=None, stream=None):
         "topk",
     )
     return lists, am
-
-
-def register_torch_ops():
-    """torch.ops.qres.{quantize_fp8, topk}: custom ops over the C ABI (the reference's device ops)"""
-    if hasattr(torch.ops, "qres") and hasattr(torch.ops.qres, "topk"):
-        return
-
-    @torch.library.custom_op("qres::quantize_fp8", mutates_args=())
-    def _q(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        return quantize_fp8(w)
-
-    @torch.library.custom_op("qres::topk", mutates_args=())
-    def _t(logits: torch.Tensor, base: int) -> tuple[torch.Tensor, torch.Tensor]:
-        return topk(logits, base)

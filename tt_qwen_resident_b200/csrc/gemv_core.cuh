@@ -1,6 +1,5 @@
-// Shared device pieces of the FP8 weight-streaming kernels (gemv_fp8.cu: one projection per launch;
-// gemv_chain.cu: the projections between two mixers as one persistent launch): the operand / shared-memory
-// geometry, the tcgen05 wrappers (cta_group::1) and the e4m3 conversions.
+// Shared device pieces of the FP8 weight-streaming kernel (gemv_fp8.cu): the operand / shared-memory geometry, the
+// tcgen05 wrappers (cta_group::1) and the e4m3 conversions.
 #pragma once
 
 #include <algorithm>

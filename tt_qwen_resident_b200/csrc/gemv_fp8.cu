@@ -774,11 +774,22 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.rc_ranks = e.rc_ranks;
     p.rc_nkb = e.rc_nkb;
     p.rc_base = p.rc_rem = 0;
+    // the counted words keep their contribution count in the low 8 bits: ranks x (CTAs over one 128-row tile)
+    // must stay below 256, for this launch's adds (EPI_XACC) and for the producer a prologue waits for
+    auto max_ctas_per_tile = [](int units, int grid, int nkb) {
+        const int b = units / grid, r = units % grid, big = r * (b + 1);
+        auto cta = [&](int u) { return u < big ? u / (b + 1) : r + (u - big) / b; };
+        int m = 0;
+        for (int t = 0; t < units / nkb; ++t) m = std::max(m, cta(t * nkb + nkb - 1) - cta(t * nkb) + 1);
+        return m;
+    };
     if (e.rc_ranks > 0) {
         if (e.racc == nullptr || e.rc_grid < 1 || e.rc_nkb < 1 || e.rc_units < e.rc_grid) return cudaErrorInvalidValue;
         p.rc_base = e.rc_units / e.rc_grid;
         p.rc_rem = e.rc_units % e.rc_grid;
+        if (e.rc_ranks * max_ctas_per_tile(e.rc_units, e.rc_grid, e.rc_nkb) >= 256) return cudaErrorInvalidValue;
     }
+    if (epi == EPI_XACC && e.xn * max_ctas_per_tile(tiles * nkb, grid, nkb) >= 256) return cudaErrorInvalidValue;
     if (e.nsrc < 1 || e.nsrc > kMaxPeers || e.p2p_n < 0 || e.p2p_n > kMaxPeers) return cudaErrorInvalidValue;
     if ((epi == EPI_P2P) != (e.p2p_n > 0) || (e.tagged != nullptr && pro != PRO_RMSNORM_ADD) ||
         ((e.tagged != nullptr || e.p2p_n > 0) && e.epoch == nullptr))

@@ -267,19 +267,99 @@ __global__ void embed_rows_kernel(const qres_tok* tok, const float* x0, const ui
     }
 }
 
-__global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, uint32_t* epoch) {
+// ------------------------------------------------------------------------------------------------ sampling draw
+// The draw of the fed token from a row's final top-32 list (keys descending, then vocab indices; key 0 = empty),
+// an integer contract with the reference's hub (sampling.hpp:77-143, bit-exact): temperature, then top-k, then
+// top-p (vLLM's order) in Q16 fixed point. Parameter words: 1 / temperature in Q16 (0 = greedy), top-k (<= 1:
+// greedy; at most 32), top-p in Q16 (65536 = off), seed. The random number hashes (seed, position), so a seeded
+// request repeats and nothing carries over between steps. All arithmetic is 32 / 64-bit integer with the
+// reference's wrap-around.
+
+// bf16 bits -> Q16.16
+__device__ __forceinline__ int32_t q16_of_bf16(uint32_t b) {
+    const int32_t e = (b >> 7) & 0xff;
+    if (e == 0) return 0;
+    const int32_t m = (b & 0x7f) | 0x80;
+    const int32_t sh = e - 118;  // value m * 2^(e - 134): m << (e - 118) in Q16
+    const int32_t v = sh >= 0 ? (sh > 22 ? (m << 22) : (m << sh)) : (sh < -31 ? 0 : (m >> -sh));
+    return (b & 0x8000) ? -v : v;
+}
+
+// exp(d) in Q16 for d <= 0 in Q16: 2^(d log2 e) with the fraction by the reference's degree-5 polynomial
+__device__ __forceinline__ uint32_t exp_q16(int32_t d) {
+    const int32_t t = (int32_t)(((int64_t)d * 94548) >> 16);
+    const int32_t n = t >> 16;
+    const uint32_t f = (uint32_t)t & 0xffffu;
+    uint32_t p = 87u;
+    p = 630u + ((p * f) >> 16);
+    p = 3638u + ((p * f) >> 16);
+    p = 15743u + ((p * f) >> 16);
+    p = 45426u + ((p * f) >> 16);
+    p = 65536u + ((p * f) >> 16);
+    return n <= -31 ? 0u : p >> -n;
+}
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+__device__ __forceinline__ uint32_t bf16_of_key(uint32_t k) { return (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu); }
+
+// list: 32 keys then 32 indices; words: the 4 parameter words; pos: the position of the row being decoded
+__device__ uint32_t draw_token(const uint32_t* list, const uint32_t* words, uint32_t pos) {
+    const uint32_t inv_temp = words[0];
+    const uint32_t k = words[1] < (uint32_t)kTopK ? words[1] : (uint32_t)kTopK;
+    if (inv_temp == 0 || k <= 1) return list[kTopK];
+    uint32_t w[kTopK];
+    const int32_t l0 = q16_of_bf16(bf16_of_key(list[0]));
+    uint32_t total = 0;
+    for (uint32_t i = 0; i < k; ++i) {
+        int64_t d = ((int64_t)(q16_of_bf16(bf16_of_key(list[i])) - l0) * (int64_t)inv_temp) >> 16;
+        d = d < -(int64_t)(64 << 16) ? -(int64_t)(64 << 16) : d;
+        w[i] = list[i] ? exp_q16((int32_t)d) : 0u;
+        total += w[i];
+    }
+    const uint32_t limit = (uint32_t)(((uint64_t)total * words[2]) >> 16);
+    uint32_t kept = 0, mass = 0;
+    while (kept < k && (kept == 0 || mass < limit)) mass += w[kept++];
+    uint32_t target = (uint32_t)(((uint64_t)mix32(words[3] ^ mix32(pos + 0x9e3779b9u)) * mass) >> 32);
+    for (uint32_t i = 0; i < kept; ++i) {
+        if (target < w[i]) return list[kTopK + i];
+        target -= w[i];
+    }
+    return list[kTopK + kept - 1];
+}
+
+// standalone draws (qres_sample): one thread per row
+__global__ void sample_kernel(int rows, const uint32_t* lists, const uint32_t* words, const int32_t* pos, int32_t* token) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < rows) token[b] = (int32_t)draw_token(lists + (size_t)b * 2 * kTopK, words + 4 * b, (uint32_t)pos[b]);
+}
+
+// out[b] = {next token, pos + 1, greedy argmax, 0}: the next token is the draw from the row's final list when
+// sampling words are bound (words [rows][4]; a row with 1 / temperature 0 or top-k <= 1 draws its argmax), else
+// the argmax. Feed mode writes it and pos + 1 into the token state (mlp_hub.cpp:414-458).
+__global__ void feed_kernel(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, uint32_t* epoch,
+                            const uint32_t* lists, const uint32_t* words) {
     pdl_launch();
     pdl_wait();
     const int b = threadIdx.x;
     if (b < rows) {
         const int a = argmax ? argmax[b] : -1;
-        const int np = tok->pos[b] + 1;
+        const int p = tok->pos[b], np = p + 1;
+        const int t = (argmax && lists && words) ? (int)draw_token(lists + (size_t)b * 2 * kTopK, words + 4 * b, (uint32_t)p) : a;
         if (out) {
-            out[b * 4 + 0] = a;
+            out[b * 4 + 0] = t;
             out[b * 4 + 1] = np;
+            out[b * 4 + 2] = a;
         }
         if (tok->feed && argmax) {
-            tok->token[b] = a;
+            tok->token[b] = t;
             tok->pos[b] = np;
         }
     }
@@ -303,6 +383,34 @@ __global__ void publish_lists_kernel(const uint32_t* __restrict__ list, int word
         __threadfence_system();
         red_release_sys_add(dst.cnt[threadIdx.x] + slot * 8, 1u);
     }
+}
+
+// ------------------------------------------------------------------------------------------------ KV rows <-> pages
+// One user's K / V rows of positions 0 .. npos-1 ([nkv][npos][256] bf16, contiguous) to or from the paged pool
+// ([pages][nkv][64][256]): position p of head j is row p % 64 of page page_table[p / 64]. One CTA per (position,
+// head, K or V), 32 threads x 16 bytes. to_pages: 1 = rows -> pool (load), 0 = pool -> rows (dump).
+__global__ void kv_rows_kernel(uint16_t* kp, uint16_t* vp, uint16_t* k, uint16_t* v, const int32_t* page_table,
+                               int npos, int nkv, int num_pages, int to_pages, uint32_t* err) {
+    const int p = blockIdx.x, j = blockIdx.y;
+    const int pg = page_table[p / kKvBlock];
+    if (pg < 0 || pg >= num_pages) {
+        if (threadIdx.x == 0) atomicOr(err, kErrBounds);
+        return;
+    }
+    uint16_t* pool = blockIdx.z ? vp : kp;
+    uint16_t* rows = blockIdx.z ? v : k;
+    uint4* a = reinterpret_cast<uint4*>(pool + (((size_t)pg * nkv + j) * kKvBlock + p % kKvBlock) * kHD);
+    uint4* b = reinterpret_cast<uint4*>(rows + ((size_t)j * npos + p) * kHD);
+    if (to_pages) a[threadIdx.x] = b[threadIdx.x];
+    else b[threadIdx.x] = a[threadIdx.x];
+}
+
+cudaError_t kv_rows_launch(uint16_t* kp, uint16_t* vp, uint16_t* k, uint16_t* v, const int32_t* page_table, int npos,
+                           int nkv, int num_pages, bool to_pages, uint32_t* err, cudaStream_t st) {
+    if (npos < 1 || nkv < 1) return cudaErrorInvalidValue;
+    kv_rows_kernel<<<dim3(npos, nkv, 2), kHD * 2 / 16, 0, st>>>(kp, vp, k, v, page_table, npos, nkv, num_pages,
+                                                                 to_pages ? 1 : 0, err);
+    return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -373,10 +481,17 @@ cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16
 }
 
 cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl,
-                        uint32_t* epoch) {
+                        uint32_t* epoch, const uint32_t* lists, const uint32_t* words) {
     cudaLaunchAttribute at[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(1), dim3(32), 0, st, at, pdl);
-    return cudaLaunchKernelEx(&cfg, feed_kernel, tok, argmax, out, rows, epoch);
+    return cudaLaunchKernelEx(&cfg, feed_kernel, tok, argmax, out, rows, epoch, lists, words);
+}
+
+cudaError_t sample_launch(int rows, const uint32_t* lists, const uint32_t* words, const int32_t* pos, int32_t* token,
+                          cudaStream_t st) {
+    if (rows < 1) return cudaErrorInvalidValue;
+    sample_kernel<<<(rows + 127) / 128, 128, 0, st>>>(rows, lists, words, pos, token);
+    return cudaGetLastError();
 }
 
 }  // namespace qres

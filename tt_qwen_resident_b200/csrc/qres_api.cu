@@ -20,7 +20,7 @@
 #include <string>
 #include <vector>
 
-#include "gemv_chain.cuh"
+#include "gemv_core.cuh"
 
 namespace qres {
 cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in, int ld_in, int epi, void* out,
@@ -56,7 +56,11 @@ size_t topk_ticket_offset(int rows, int nblk);
 cudaError_t embed_rows_launch(const qres_tok* tok, const float* x0, const uint16_t* embed, int vocab, float* x, int rows,
                               uint32_t* err, cudaStream_t st, bool pdl);
 cudaError_t feed_launch(qres_tok* tok, const int32_t* argmax, int32_t* out, int rows, cudaStream_t st, bool pdl,
-                        uint32_t* epoch);
+                        uint32_t* epoch, const uint32_t* lists, const uint32_t* words);
+cudaError_t sample_launch(int rows, const uint32_t* lists, const uint32_t* words, const int32_t* pos, int32_t* token,
+                          cudaStream_t st);
+cudaError_t kv_rows_launch(uint16_t* kp, uint16_t* vp, uint16_t* k, uint16_t* v, const int32_t* page_table, int npos,
+                           int nkv, int num_pages, bool to_pages, uint32_t* err, cudaStream_t st);
 }  // namespace qres
 
 using namespace qres;
@@ -145,6 +149,7 @@ struct qres_ctx {
     qres_weight fc = {};  // the MTP draft layer's fc (QRES_W_FC)
     bool has_fc = false;
     const float *cos_tab = nullptr, *sin_tab = nullptr;
+    const uint32_t* sampling = nullptr;  // [rows][4] words of the fed token's draw (qres_bind_sampling), or greedy
     int max_pos = 0;
     qres_io io = {};
     bool has_io = false;
@@ -163,12 +168,9 @@ struct qres_ctx {
     int topk_blk = 1;
     void* gemv_work = nullptr;
     size_t gemv_work_bytes = 0;
-    uint2 *xch = nullptr, *atag = nullptr;
     // one rank: the out-projection's, gate|up's and the down-projection's fixed-point sums (EPI_ACC), and the
     // in-projection's (read by the mixers), which follows the out-projection's in memory
     long long* acc[4] = {};
-    void* chain_work = nullptr;
-    size_t chain_work_bytes = 0;
     ncclComm_t comm = nullptr;
     // peer exchange (qres_p2p_alloc / qres_p2p_open): this rank's window and every rank's window as mapped here
     uint8_t* p2p_local = nullptr;
@@ -214,8 +216,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, xch, atag, chain,
-        chain_bytes, acc[4], total;
+    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, acc[4], total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -241,12 +242,6 @@ Carve carve(const qres_ctx* c) {
     k.topk = take(c->vocab_local ? topk_workspace_bytes(R, c->topk_blk) : 0);
     k.gemv_bytes = gemv_workspace_bytes(2 * c->sm_count);
     k.gemv = take(k.gemv_bytes);
-    // the chained projections (gemv_chain.cu): the one-rank exchange slots [3][rows][5120] and gate|up's tagged
-    // SwiGLU output [rows][17408 / n], as tagged 8-byte words, and the chain's tickets / partial sums
-    k.xch = take((size_t)3 * R * kHidden * 8);
-    k.atag = take((size_t)R * c->ic * 8);
-    k.chain_bytes = chain_workspace_bytes(2 * c->sm_count);
-    k.chain = take(k.chain_bytes);
     // fixed-point accumulators of the one-rank step (int64): out-projection [rows][5120] and right behind it the
     // in-projection [rows][ld_y] (one range for the launch that zeroes both), gate|up [rows][2 x 17408],
     // down-projection [rows][5120]
@@ -291,7 +286,7 @@ qres_status qres_create(const qres_config* cfg, int32_t rank, int32_t nranks, qr
     if (cfg->rows < 1 || cfg->rows > QRES_MAX_ROWS || cfg->layers < 1)
         return fail(nullptr, QRES_ERR_ARG, "qres_create: rows %d, layers %d", cfg->rows, cfg->layers);
     if (cfg->vocab % nranks) return fail(nullptr, QRES_ERR_ARG, "qres_create: vocab %d not divisible by %d", cfg->vocab, nranks);
-    if (cfg->flags & ~(QRES_FLAG_VERIFY | QRES_FLAG_CHAIN | QRES_FLAG_TILE_FINISH))
+    if (cfg->flags & ~(QRES_FLAG_VERIFY | QRES_FLAG_TILE_FINISH))
         return fail(nullptr, QRES_ERR_ARG, "qres_create: unknown flags %#x", cfg->flags);
     if ((cfg->flags & QRES_FLAG_VERIFY) && (cfg->rows < 2 || cfg->rows + 3 > QRES_HIST_SLOTS))
         return fail(nullptr, QRES_ERR_ARG, "qres_create: a verify step has 2..%d rows, not %d", QRES_HIST_SLOTS - 3,
@@ -400,6 +395,79 @@ qres_status qres_bind_state(qres_ctx* c, int32_t layer, const qres_layer_state* 
     return QRES_OK;
 }
 
+// ---- decode state in and out (State / load_state, model.py:151-174, 1447-1470) ----
+
+static qres_status gdn_layer_state(qres_ctx* c, int32_t layer, int32_t user, const char* what, float** st,
+                                   size_t* bytes) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "%s: null context", what);
+    if (layer < 0 || layer >= c->cfg.layers || is_attn(c, layer) || !c->layers[layer].has_st)
+        return fail(c, QRES_ERR_ARG, "%s: layer %d is not a bound GDN layer", what, layer);
+    if (user < 0 || user >= c->cfg.rows) return fail(c, QRES_ERR_ARG, "%s: user %d of %d", what, user, c->cfg.rows);
+    *bytes = (size_t)c->nv * kDK * kDV * 4;
+    *st = c->layers[layer].st.gdn_state + (size_t)user * c->nv * kDK * kDV;
+    return QRES_OK;
+}
+
+qres_status qres_load_gdn_state(qres_ctx* c, int32_t layer, int32_t user, const float* state, const uint16_t* hist3,
+                                int32_t pos, void* stream) {
+    float* dst = nullptr;
+    size_t bytes = 0;
+    qres_status s = gdn_layer_state(c, layer, user, "qres_load_gdn_state", &dst, &bytes);
+    if (s) return s;
+    if (!state || pos < 0) return fail(c, QRES_ERR_ARG, "qres_load_gdn_state: state null or pos %d", pos);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CU(c, cudaMemcpyAsync(dst, state, bytes, cudaMemcpyDeviceToDevice, st));
+    if (hist3) {
+        // the history ring of this user (a verify context's single user); position q in slot q % QRES_HIST_SLOTS
+        const int conv = 2 * c->nk * kDK + c->nv * kDV;
+        const int hu = (c->cfg.flags & QRES_FLAG_VERIFY) ? 0 : user;
+        uint16_t* ring = c->layers[layer].st.conv_hist + (size_t)hu * QRES_HIST_SLOTS * conv;
+        for (int age = 0; age < 3; ++age) {
+            const int slot = ((pos - 3 + age) % QRES_HIST_SLOTS + QRES_HIST_SLOTS) % QRES_HIST_SLOTS;
+            CU(c, cudaMemcpyAsync(ring + (size_t)slot * conv, hist3 + (size_t)age * conv, (size_t)conv * 2,
+                                  cudaMemcpyDeviceToDevice, st));
+        }
+    }
+    return QRES_OK;
+}
+
+qres_status qres_dump_gdn_state(qres_ctx* c, int32_t layer, int32_t user, float* state, void* stream) {
+    float* src = nullptr;
+    size_t bytes = 0;
+    qres_status s = gdn_layer_state(c, layer, user, "qres_dump_gdn_state", &src, &bytes);
+    if (s) return s;
+    if (!state) return fail(c, QRES_ERR_ARG, "qres_dump_gdn_state: null destination");
+    CU(c, cudaMemcpyAsync(state, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+    return QRES_OK;
+}
+
+static qres_status kv_rows(qres_ctx* c, int32_t layer, int32_t user, uint16_t* k, uint16_t* v, int32_t npos,
+                           void* stream, bool load) {
+    const char* what = load ? "qres_load_kv" : "qres_dump_kv";
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "%s: null context", what);
+    if (layer < 0 || layer >= c->cfg.layers || !is_attn(c, layer) || !c->layers[layer].has_st)
+        return fail(c, QRES_ERR_ARG, "%s: layer %d is not a bound attention layer", what, layer);
+    if (user < 0 || user >= c->cfg.rows || !k || !v || npos < 1 || npos > c->cfg.max_pages * kKvBlock)
+        return fail(c, QRES_ERR_ARG, "%s: user %d, %d positions (at most %d)", what, user, npos,
+                    c->cfg.max_pages * kKvBlock);
+    if (!c->has_io || !c->io.page_table || !c->err) return fail(c, QRES_ERR_STATE, "%s before bind_io / bind_workspace", what);
+    const Layer& L = c->layers[layer];
+    const int32_t* pt = c->io.page_table + (size_t)((c->cfg.flags & QRES_FLAG_VERIFY) ? 0 : user) * c->cfg.max_pages;
+    CU(c, kv_rows_launch(L.st.k_pool, L.st.v_pool, k, v, pt, npos, c->nkv, c->cfg.num_pages, load, c->err,
+                         static_cast<cudaStream_t>(stream)));
+    return QRES_OK;
+}
+
+qres_status qres_load_kv(qres_ctx* c, int32_t layer, int32_t user, const uint16_t* k, const uint16_t* v, int32_t npos,
+                         void* stream) {
+    return kv_rows(c, layer, user, const_cast<uint16_t*>(k), const_cast<uint16_t*>(v), npos, stream, true);
+}
+
+qres_status qres_dump_kv(qres_ctx* c, int32_t layer, int32_t user, uint16_t* k, uint16_t* v, int32_t npos,
+                         void* stream) {
+    return kv_rows(c, layer, user, k, v, npos, stream, false);
+}
+
 qres_status qres_bind_rope(qres_ctx* c, const float* cos_tab, const float* sin_tab, int32_t max_pos) {
     if (!c || !cos_tab || !sin_tab || max_pos < 1) return fail(c, QRES_ERR_ARG, "qres_bind_rope: bad argument");
     c->cos_tab = cos_tab;
@@ -414,6 +482,13 @@ qres_status qres_bind_io(qres_ctx* c, const qres_io* io) {
         return fail(c, QRES_ERR_ARG, "qres_bind_io: the lm_head needs logits, topk and out");
     c->io = *io;
     c->has_io = true;
+    return QRES_OK;
+}
+
+qres_status qres_bind_sampling(qres_ctx* c, const uint32_t* words) {
+    if (!c) return fail(nullptr, QRES_ERR_ARG, "null context");
+    if (words && !c->cfg.vocab) return fail(c, QRES_ERR_ARG, "qres_bind_sampling: sampling needs an lm_head");
+    c->sampling = words;  // a captured graph holds the pointer it was captured with: bind before qres_capture
     return QRES_OK;
 }
 
@@ -447,10 +522,6 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->topk_work = c->vocab_local ? (void*)(w + k.topk) : nullptr;
     c->gemv_work = w + k.gemv;
     c->gemv_work_bytes = k.gemv_bytes;
-    c->xch = reinterpret_cast<uint2*>(w + k.xch);
-    c->atag = reinterpret_cast<uint2*>(w + k.atag);
-    c->chain_work = w + k.chain;
-    c->chain_work_bytes = k.chain_bytes;
     for (int i = 0; i < 4; ++i) c->acc[i] = reinterpret_cast<long long*>(w + k.acc[i]);
     return QRES_OK;
 }
@@ -536,6 +607,14 @@ qres_status qres_nccl_init(qres_ctx* c, const char* libpath, const void* id128) 
     return QRES_OK;
 }
 
+// the fixed-point accumulators (EPI_ACC; between ranks the counted exchange): with an lm_head, up to 2 rows, not
+// switched off by QRES_FLAG_TILE_FINISH, and across ranks only over the peer window with native peer atomics
+static bool uses_accumulators(const qres_ctx* c) {
+    const bool tp = c->nranks > 1;
+    return !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && c->cfg.rows <= 2 &&
+           (!tp || (c->p2p_on && c->p2p_atomics));
+}
+
 static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     const int R = c->cfg.rows, n = c->nranks;
     const bool tp = n > 1;
@@ -579,8 +658,6 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     if (!c->has_fc) {
         STEP(embed_rows_launch(c->io.tok, c->io.x0, c->io.embed, c->cfg.vocab, cur, R, c->err, st, true), "rows in");
     }
-    // the chained projections (gemv_chain.cu): with an lm_head, and the peer exchange when nranks > 1
-    const bool chain = c->cfg.vocab > 0 && (c->cfg.flags & QRES_FLAG_CHAIN) && (!tp || p2p) && R <= 4;
     bool pending = false;  // all-reduced partials waiting to be added to cur
     int xchg = 0;          // row-parallel exchanges issued so far in this step (peer exchange: slot xchg % 2)
     auto allreduce = [&]() -> qres_status {
@@ -631,8 +708,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     //   XA / XC (in the peer window), and the next prologue reads them once each word holds all contributions.
     //   In-proj zeroes accB, out-proj XC, gate|up accD, down XA -- the exchange buffers with a system-scope fence:
     //   peers add into them only after this rank's next contributions, which follow the fence.
-    const bool accm = !chain && !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && R <= 2 &&
-                      (!tp || (p2p && c->p2p_atomics));
+    const bool accm = uses_accumulators(c);
     long long* const accB = c->acc[1];
     long long* const accD = c->acc[3];
     long long* xa_at[8] = {};
@@ -756,7 +832,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                              nullptr, add ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
                  "in-proj");
             if (add) std::swap(cur, other);
-        } else if (!chain || l == 0) {  // chained: layers > 0 get theirs from the previous chain
+        } else {
             s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
             if (s) return s;
         }
@@ -772,71 +848,6 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             STEP(gdn_launch(n, R, c->y, c->ld_y, pos, L.taps, L.dt, L.neg_a, L.norm_w, L.st.gdn_state, L.st.conv_hist,
                             c->o, mcopy, c->err, st, true, pf, pf_bytes, verify, &c->io.tok->slot, accm ? accD : nullptr),
                  "gdn");
-        }
-        if (chain) {
-            // out-proj, gate|up, down and the next in-proj (or the lm_head) as one persistent launch; exchange j of
-            // the step (out 2l, down 2l + 1) carries tag epoch * 2L + j + 1, gate|up's output epoch * L + l + 1
-            const int L2 = 2 * c->cfg.layers;
-            ChainParams cp = {};
-            cp.nphase = 4;
-            cp.users = R;
-            cp.nsrc = n;
-            cp.epoch = c->epoch;
-            cp.rank = c->rank;
-            cp.set_mul = (uint32_t)L2;
-            cp.src_words = (size_t)R * kHidden;
-            cp.slot_words = (size_t)(p2p ? 8 : 1) * R * kHidden;
-            for (int r = 0; r < n; ++r) cp.xbase[r] = p2p ? reinterpret_cast<uint2*>(c->p2p_peer[r] + pl.data) : c->xch;
-            auto phase = [&](ChainPhase& ph, const qres_weight& w) {
-                ph.w = static_cast<const uint8_t*>(w.data);
-                ph.table = reinterpret_cast<const uint8_t*>(w.uscale);
-                ph.rows = w.rows;
-                ph.tiles = w.rows_pad / 128;
-                ph.K = w.K;
-                ph.nkb = w.K / 128;
-            };
-            ChainPhase& po = cp.ph[0];
-            phase(po, L.w[QRES_W_OUT]);
-            po.in_kind = CIN_BF16;
-            po.in_bf16 = c->o;
-            po.out_kind = COUT_PARTIAL;
-            po.ld_out = kHidden;
-            po.out_add = (uint32_t)(2 * l + 1);
-            ChainPhase& pg = cp.ph[1];
-            phase(pg, L.w[QRES_W_GATEUP]);
-            pg.in_kind = CIN_NORM;
-            pg.x = cur;
-            pg.nsets = 1;
-            pg.set_add[0] = (uint32_t)(2 * l + 1);
-            pg.out_kind = COUT_SILU_TAGGED;
-            pg.out = c->atag;
-            pg.ld_out = c->ic;
-            pg.out_mul = (uint32_t)c->cfg.layers;
-            pg.out_add = (uint32_t)(l + 1);
-            ChainPhase& pd = cp.ph[2];
-            phase(pd, L.w[QRES_W_DOWN]);
-            pd.in_kind = CIN_TAGGED_BF16;
-            pd.in_tagged = c->atag;
-            pd.in_mul = (uint32_t)c->cfg.layers;
-            pd.in_add = (uint32_t)(l + 1);
-            pd.out_kind = COUT_PARTIAL;
-            pd.ld_out = kHidden;
-            pd.out_add = (uint32_t)(2 * l + 2);
-            ChainPhase& pn = cp.ph[3];
-            const bool last = l == c->cfg.layers - 1;
-            phase(pn, last ? c->head : c->layers[l + 1].w[is_attn(c, l + 1) ? QRES_W_ATTN_IN : QRES_W_GDN_IN]);
-            pn.in_kind = CIN_NORM;
-            pn.x = cur;
-            pn.nsets = 2;
-            pn.set_add[0] = (uint32_t)(2 * l + 1);
-            pn.set_add[1] = (uint32_t)(2 * l + 2);
-            pn.x_out = other;
-            pn.out_kind = COUT_BF16;
-            pn.out = last ? static_cast<void*>(c->io.logits) : static_cast<void*>(c->y);
-            pn.ld_out = last ? c->vocab_local : c->ld_y;
-            STEP(chain_launch(cp, 2 * c->sm_count, c->sm_count, c->chain_work, c->chain_work_bytes, st, true), "chain");
-            std::swap(cur, other);
-            continue;
         }
         if (accm) {
             const qres_weight& wo = L.w[QRES_W_OUT];
@@ -893,10 +904,8 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         if (s) return s;
     }
     if (c->cfg.vocab) {
-        if (!chain) {
-            qres_status s = norm_gemv(c->head, 0, c->io.logits, c->vocab_local, "lm_head");
-            if (s) return s;
-        }
+        qres_status s = norm_gemv(c->head, 0, c->io.logits, c->vocab_local, "lm_head");
+        if (s) return s;
         const int base = c->rank * c->vocab_local;
         if (!tp) {
             STEP(topk_launch(R, c->io.logits, c->vocab_local, c->vocab_local, base, c->io.topk, c->argmax, c->topk_work,
@@ -926,9 +935,9 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             if (r != ncclSuccess) return fail(c, QRES_ERR_COMM, "ncclAllGather: %d", (int)r);
             STEP(merge_lists_launch(c->gathered, n, R, c->io.topk, c->argmax, st, true), "merge");
         }
-        STEP(feed_launch(c->io.tok, c->argmax, c->io.out, R, st, true, c->epoch), "feed");
+        STEP(feed_launch(c->io.tok, c->argmax, c->io.out, R, st, true, c->epoch, c->io.topk, c->sampling), "feed");
     } else {
-        STEP(feed_launch(c->io.tok, nullptr, nullptr, R, st, true, c->epoch), "feed");
+        STEP(feed_launch(c->io.tok, nullptr, nullptr, R, st, true, c->epoch, nullptr, nullptr), "feed");
     }
     if (cur != c->io.x) CU(c, cudaMemcpyAsync(c->io.x, cur, (size_t)R * kHidden * 4, cudaMemcpyDeviceToDevice, st));
 #undef STEP
@@ -991,6 +1000,13 @@ qres_status qres_check(qres_ctx* c, void* stream) {
 }
 
 int32_t qres_step_launches(const qres_ctx* c) { return c ? c->launches : 0; }
+
+int32_t qres_exchange_mode(const qres_ctx* c) {
+    if (!c) return -1;
+    if (c->nranks == 1) return QRES_XCHG_NONE;
+    if (c->p2p_on) return uses_accumulators(c) ? QRES_XCHG_COUNTED : QRES_XCHG_TAGGED;
+    return c->comm ? QRES_XCHG_NCCL : QRES_XCHG_NONE;
+}
 
 // ---- single kernels ----
 
@@ -1077,6 +1093,14 @@ qres_status qres_topk(int32_t rows, const uint16_t* logits, int32_t n_logits, in
     cudaError_t e = topk_launch(rows, logits, n_logits, n_logits, base, lists, argmax, work, nblk,
                                 static_cast<cudaStream_t>(stream), false);
     if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_topk: %s", cudaGetErrorString(e));
+    return QRES_OK;
+}
+
+qres_status qres_sample(int32_t rows, const uint32_t* lists, const uint32_t* words, const int32_t* pos, int32_t* token,
+                        void* stream) {
+    if (!lists || !words || !pos || !token || rows < 1) return fail(nullptr, QRES_ERR_ARG, "qres_sample: bad argument");
+    cudaError_t e = sample_launch(rows, lists, words, pos, token, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_sample: %s", cudaGetErrorString(e));
     return QRES_OK;
 }
 

@@ -17,7 +17,7 @@ import math
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, ops
 from .weights import CONV_CH, DK, DV, HD, HIDDEN, NKV, NV, RankDims, shard, stack_matrices
 
 ROPE_THETA = 10_000_000.0
@@ -56,14 +56,16 @@ class ResidentModel:
         p2p=False,
         verify=False,
         fc=None,
-        chain=False,
         tile_finish=False,
+        share=None,
     ):
         """w: canonical FP8 weights (weights.random_canonical / canonical_from_*): lists per kind; layer l of a
         kind uses copy (k-th layer of that kind) % copies (mlp / out: l % copies), as the reference's
         random_weights copies. state_copies: (gdn, attn) decode states (default one per layer; fewer share a
         state between layers like the reference's State copies). embed: [vocab, 5120] bf16 table for token
-        rows (device-fed decode). page_table: [batch, max_pages] int32 (default: user b's pages contiguous)."""
+        rows (device-fed decode). page_table: [batch, max_pages] int32 (default: user b's pages contiguous).
+        share: another ResidentModel of the same layers, rank and vocab whose device weights this one uses (w is
+        then ignored; e.g. a batch-8 model beside a batch-1 one without a second copy of the weights)."""
         self.device = torch.device(device)
         self.layers, self.interval, self.batch = layers, interval, batch
         # verify (model.py:416-457): the batch rows are consecutive positions of ONE user (row r sees rows < r);
@@ -74,8 +76,12 @@ class ResidentModel:
             assert state_copies is None, "verify: one GDN state / KV cache per layer"
         self.users = batch
         self.rank, self.nranks = rank, nranks
-        self.lm_head = lm_head and w.get("head") is not None
-        vocab = w["head"].shape[0] if self.lm_head else 0
+        if share is not None:
+            self.lm_head = lm_head and share.lm_head
+            vocab = share.vocab if self.lm_head else 0
+        else:
+            self.lm_head = lm_head and w.get("head") is not None
+            vocab = w["head"].shape[0] if self.lm_head else 0
         self.vocab = vocab
         self.d = d = RankDims(rank, nranks, vocab)
         self.max_pos = max_pos
@@ -85,13 +91,10 @@ class ResidentModel:
         gc, ac = state_copies or (self.n_gdn, self.n_attn)
         self.state_copies = (max(gc, 1) if self.n_gdn else 0, max(ac, 1) if self.n_attn else 0)
         L = _lib.lib()
-        # chain: the projections between two mixers as one persistent launch (gemv_chain.cu) where the library
-        # can (lm_head, <= 4 rows, peer exchange when nranks > 1); False (default): one launch per projection
         # tile_finish: split projection tiles finished by their last CTA (ticket) rather than summed in the
         # fixed-point accumulators the library uses at one rank with up to 2 rows
         flags = (
             (_lib.QRES_FLAG_VERIFY if self.verify else 0)
-            | (_lib.QRES_FLAG_CHAIN if chain else 0)
             | (_lib.QRES_FLAG_TILE_FINISH if tile_finish else 0)
         )
         cfg = _lib.Config(layers, interval, vocab, batch, self.max_pages, batch * self.max_pages, sm_count, flags)
@@ -100,7 +103,38 @@ class ResidentModel:
         self.ctx = h
         self._keep = []
         dev = self.device
-        # ---- weights: the rank's slices, re-laid for the GEMV
+        # ---- weights: the rank's slices, re-laid for the GEMV (or another model's, same layers / rank / vocab)
+        if share is not None:
+            assert (share.layers, share.interval, share.rank, share.nranks, share.vocab) == (layers, interval, rank,
+                                                                                           nranks, vocab)
+            assert fc is None and share.device == self.device
+            w = None
+        self._init_weights(w, share, fc)
+        self.weight_bytes = self._count_weight_bytes()
+        self._init_buffers(page_table, embed)
+        # ---- bind
+        self._bind()
+        sz = ctypes.c_size_t()
+        _lib.check(L.qres_workspace_size(self.ctx, ctypes.byref(sz)), self.ctx, "workspace size")
+        self.ws = torch.zeros(sz.value, dtype=torch.uint8, device=dev)
+        _lib.check(L.qres_bind_workspace(self.ctx, _lib.ptr(self.ws), sz.value), self.ctx, "bind workspace")
+        if nranks > 1 and nccl_id is not None:
+            buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            _lib.check(L.qres_nccl_init(self.ctx, None, buf), self.ctx, "nccl init")
+        if nranks > 1 and p2p:
+            self._open_p2p()
+        elif nranks > 1 and nccl_id is None:
+            raise ValueError("nranks > 1 needs p2p=True (fused peer exchange) or the NCCL id (see nccl_unique_id)")
+        self.trace = False
+        self._initial = None
+
+    def _init_weights(self, w, share, fc):
+        d, dev = self.d, self.device
+        if share is not None:
+            for k in ("w_gdn", "gdn_params", "w_attn", "attn_params", "w_out", "w_gu", "w_down", "w_head"):
+                setattr(self, k, getattr(share, k))
+            self.w_fc = None
+            return
         self.w_gdn = [shard(g["Win"], d.gdn_rows()) for g in w["gdn"]] if self.n_gdn else []
         self.gdn_params = [
             dict(
@@ -124,13 +158,15 @@ class ResidentModel:
         # embedding row, h the rows of h_d (set_hidden: a previous step's last x); fc canonical [5120, 10240]
         # FP8 with the pre-fc norm weights folded into its columns
         if fc is not None:
-            assert nranks == 1, "the fc (MTP draft layer) runs on one rank"
+            assert self.nranks == 1, "the fc (MTP draft layer) runs on one rank"
             self.w_fc = shard(fc)
         else:
             self.w_fc = None
-        self.weight_bytes = self._count_weight_bytes()
+
+    def _init_buffers(self, page_table, embed):
+        d, dev, max_pos = self.d, self.device, self.max_pos
         # ---- decode state (per state copy)
-        R = batch
+        R = self.batch
         self.gdn_state = [torch.zeros(R, d.nv, DK, DV, device=dev) for _ in range(self.state_copies[0])]
         self.conv_hist = [
             torch.zeros(R, _lib.QRES_HIST_SLOTS, d.conv, dtype=torch.bfloat16, device=dev)
@@ -151,24 +187,10 @@ class ResidentModel:
         self.out_d = torch.zeros(R, 4, dtype=torch.int32, device=dev)
         self.mixer_d = torch.zeros(R, d.gv, dtype=torch.bfloat16, device=dev)
         self.h_d = torch.zeros(R, HIDDEN, device=dev)  # the fc's hidden rows (MTP draft layer)
+        self.sampling_d = torch.zeros(R, 4, dtype=torch.int32, device=dev)  # the draw's words (greedy: all 0)
         self.embed = embed.to(dev).bfloat16().contiguous() if embed is not None else None
         cos, sin = rope_table(max_pos)
         self.cos_d, self.sin_d = cos.to(dev), sin.to(dev)
-        # ---- bind
-        self._bind()
-        sz = ctypes.c_size_t()
-        _lib.check(L.qres_workspace_size(self.ctx, ctypes.byref(sz)), self.ctx, "workspace size")
-        self.ws = torch.zeros(sz.value, dtype=torch.uint8, device=dev)
-        _lib.check(L.qres_bind_workspace(self.ctx, _lib.ptr(self.ws), sz.value), self.ctx, "bind workspace")
-        if nranks > 1 and nccl_id is not None:
-            buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
-            _lib.check(L.qres_nccl_init(self.ctx, None, buf), self.ctx, "nccl init")
-        if nranks > 1 and p2p:
-            self._open_p2p()
-        elif nranks > 1 and nccl_id is None:
-            raise ValueError("nranks > 1 needs p2p=True (fused peer exchange) or the NCCL id (see nccl_unique_id)")
-        self.trace = False
-        self._initial = None
 
     def _open_p2p(self):
         """the fused peer exchange: allocate this rank's window, all-gather the CUDA IPC handles over the default
@@ -197,8 +219,10 @@ class ResidentModel:
 
     def _bind(self):
         L, c = _lib.lib(), self.ctx
+        self._state_layer = {}  # (kind, state copy) -> the first layer bound to it (the state entry points' layer)
         for l in range(self.layers):
             wc, sc = self._layer_copy(l)
+            self._state_layer.setdefault(("attn" if is_attn(l, self.interval) else "gdn", sc), l)
             m = l % len(self.w_out)
             if is_attn(l, self.interval):
                 _lib.check(L.qres_load_weights(c, l, _lib.W_ATTN_IN, ctypes.byref(self.w_attn[wc].cstruct())), c, "w")
@@ -236,6 +260,9 @@ class ResidentModel:
             self.h_d.data_ptr() if self.w_fc is not None else 0,
         )
         _lib.check(L.qres_bind_io(c, ctypes.byref(io)), c, "io")
+        ops.bind_context(c, self.tok_d, self.x_d, self.out_d)
+        if self.lm_head:
+            _lib.check(L.qres_bind_sampling(c, _lib.ptr(self.sampling_d)), c, "sampling")
 
     def set_hidden(self, h, stream=None):
         """the hidden rows the next step's fc reads (MTP draft layer): a [rows, 5120] fp32 device tensor, e.g.
@@ -300,14 +327,10 @@ class ResidentModel:
 
     def step(self, tok=None, stream=None):
         """one decode step (async); tok None: continue from the token state the previous step fed (feed mode)"""
-        if tok is not None:
-            self.write_token_state(tok)
-        s = _lib.stream_ptr(stream)
-        L = _lib.lib()
-        if self.trace:
-            _lib.check(L.qres_replay(self.ctx, s), self.ctx, "replay")
-        else:
-            _lib.check(L.qres_decode_step(self.ctx, s), self.ctx, "decode step")
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
+            if tok is not None:
+                self.write_token_state(tok)
+            torch.ops.qres.decode_step(self.ctx.value, self.tok_d, self.x_d, self.out_d, self.trace)
 
     def check(self, stream=None):
         """synchronise and raise if a kernel of the step reported an error (timeout / index out of range)"""
@@ -317,6 +340,11 @@ class ResidentModel:
     def launches(self):
         """kernels of libqres one step launches"""
         return _lib.lib().qres_step_launches(self.ctx)
+
+    @property
+    def exchange(self):
+        """the exchange between ranks the step uses: "none" (one rank), "nccl", "tagged" or "counted" words"""
+        return _lib.XCHG_NAMES[_lib.lib().qres_exchange_mode(self.ctx)]
 
     def capture_trace(self, stream=None):
         """record one step as a CUDA graph (model.py:1485-1492); step() then replays it"""
@@ -354,13 +382,34 @@ class ResidentModel:
 
     def argmax(self):
         """vocab index of the largest logit, the smallest index on ties (model.py:1558-1573); a list for batch > 1"""
-        a = self.out_d[:, 0].cpu().tolist()
+        a = self.out_d[:, 2].cpu().tolist()
         return a[0] if self.batch == 1 else a
 
-    def fed_token(self):
-        """(token, position) the last step fed into the next one"""
-        o = self.out_d[0].cpu().tolist()
+    def fed_token(self, user=0):
+        """(token, position) the last step fed into the next one: the greedy pick, or the draw when sampling is set"""
+        o = self.out_d[user].cpu().tolist()
         return int(o[0]), int(o[1])
+
+    # ------------------------------------------------------------------------------------------ sampling
+    @staticmethod
+    def sampling_words(temperature=0.0, top_k=1, top_p=1.0, seed=0):
+        """the draw's 4 parameter words (model.py:1528-1536): 1 / temperature in Q16 (0 = greedy), top_k (< 1: all
+        32; 1 = greedy), top_p in Q16, seed"""
+        top_k = TOP_K if top_k < 1 else min(int(top_k), TOP_K)
+        inv = min(round(65536 / temperature), 2**31 - 1) if temperature > 0 else 0
+        return [inv, top_k, min(max(round(top_p * 65536), 1), 65536), int(seed) & 0xFFFFFFFF]
+
+    def set_sampling(self, temperature=0.0, top_k=1, top_p=1.0, seed=None, user=None):
+        """the parameters of the fed token's draw (model.py:1538-1551), read by every later step until set again
+        (also a captured graph's replays: the words live in a bound device buffer); user None sets every row.
+        seed None picks one."""
+        assert self.lm_head, "sampling draws from the lm_head's top-32 list"
+        if seed is None:
+            seed = int(np.random.randint(0, 2**32, dtype=np.uint64))
+        w = torch.from_numpy(np.array(self.sampling_words(temperature, top_k, top_p, seed), dtype=np.uint32).view(np.int32))
+        rows = range(self.batch) if user is None else [user]
+        for r in rows:
+            self.sampling_d[r].copy_(w, non_blocking=False)
 
     # ------------------------------------------------------------------------------------------ state
     def load_state(self, st, user=0, slot=0):
@@ -371,29 +420,40 @@ class ResidentModel:
         ch = d.conv_channels()
         if self.verify:
             assert user == 0
+        L, s = _lib.lib(), _lib.stream_ptr()
+        keep = []  # sources stay alive until the copies have run
         for c in range(self.state_copies[0]):
             if c < len(st.gdn):
-                self.gdn_state[c][slot if self.verify else user].copy_(st.gdn[c][d.r * d.nv : (d.r + 1) * d.nv].to(dev))
-                h = st.hist[c][:, ch].to(dev).bfloat16()
-                for age in range(3):
-                    ring = (st.pos - 3 + age) % _lib.QRES_HIST_SLOTS
-                    self.conv_hist[c][user, ring] = h[age]
+                S = st.gdn[c][d.r * d.nv : (d.r + 1) * d.nv].to(dev).contiguous()
+                h = st.hist[c][:, ch].to(dev).bfloat16().contiguous()
+                keep += [S, h]
+                _lib.check(L.qres_load_gdn_state(self.ctx, self._state_layer[("gdn", c)], slot if self.verify else user,
+                                                 _lib.ptr(S), _lib.ptr(h), st.pos, s), self.ctx, "load gdn state")
         for c in range(self.state_copies[1]):
-            if c < len(st.K):
-                P = min(st.pos, st.K[c].shape[1])
-                pt = self.page_table[user].cpu()
-                for kv, pool in ((st.K[c], self.k_pool[c]), (st.V[c], self.v_pool[c])):
-                    src = kv[d.kv0 : d.kv0 + d.nkv, :P].to(dev).bfloat16()  # [nkv, P, 256]
-                    npg = -(-P // 64)
-                    padded = torch.zeros(d.nkv, npg * 64, HD, dtype=torch.bfloat16, device=dev)
-                    padded[:, :P] = src
-                    pages = padded.view(d.nkv, npg, 64, HD).permute(1, 0, 2, 3)
-                    pool[pt[:npg].long().to(dev)] = pages
-        torch.cuda.synchronize(dev)
+            P = min(st.pos, st.K[c].shape[1]) if c < len(st.K) else 0
+            if P > 0:
+                k = st.K[c][d.kv0 : d.kv0 + d.nkv, :P].to(dev).bfloat16().contiguous()  # [nkv, P, 256]
+                v = st.V[c][d.kv0 : d.kv0 + d.nkv, :P].to(dev).bfloat16().contiguous()
+                keep += [k, v]
+                _lib.check(L.qres_load_kv(self.ctx, self._state_layer[("attn", c)], user, _lib.ptr(k), _lib.ptr(v), P, s),
+                           self.ctx, "load kv")
+        self.check()
 
     def dump_gdn_state(self, copy=0, user=0):
-        """GDN state of layer copy `copy`: user `user`'s, or (verify) state slot `user`"""
-        return self.gdn_state[copy][user].cpu()
+        """GDN state [48/n, 128, 128] of state copy `copy`: user `user`'s, or (verify) state slot `user`"""
+        out = torch.empty(self.d.nv, DK, DV, device=self.device)
+        _lib.check(_lib.lib().qres_dump_gdn_state(self.ctx, self._state_layer[("gdn", copy)], user, _lib.ptr(out),
+                                                   _lib.stream_ptr()), self.ctx, "dump gdn state")
+        return out.cpu()
+
+    def dump_kv(self, copy, npos, user=0):
+        """(K, V) rows of positions 0 .. npos-1 of attention state copy `copy`, user `user`: bf16 [nkv, npos, 256]"""
+        k = torch.empty(self.d.nkv, npos, HD, dtype=torch.bfloat16, device=self.device)
+        v = torch.empty_like(k)
+        _lib.check(_lib.lib().qres_dump_kv(self.ctx, self._state_layer[("attn", copy)], user, _lib.ptr(k), _lib.ptr(v),
+                                           npos, _lib.stream_ptr()), self.ctx, "dump kv")
+        self.check()
+        return k.cpu(), v.cpu()
 
     def kv_rows(self, copy, positions, user=0, which="K"):
         """rows of the paged cache at positions: [nkv, len, 256] float"""
@@ -410,6 +470,7 @@ class ResidentModel:
     def close(self):
         if getattr(self, "ctx", None):
             self.release_trace()
+            ops.unbind_context(self.ctx)
             _lib.lib().qres_destroy(self.ctx)
             self.ctx = None
 
