@@ -226,6 +226,13 @@ QRES_API qres_status qres_release_graph(qres_ctx* ctx);
 /* Synchronise `stream` and read the device error word; QRES_ERR_DEVICE (with a message) when a kernel of the
  * step reported a timeout or an out-of-range index. The word is cleared. */
 QRES_API qres_status qres_check(qres_ctx* ctx, void* stream);
+/* One bounded wait of the kind the peer exchange runs on a peer's counter (the next projection waiting for the
+ * other ranks' partial sums, mlp_hub.cpp:309-364): poll the device word `flag` until it reaches `want`, at most
+ * `polls` times (each with a short sleep); if it does not, set the context's error word (timeout and peer bits),
+ * which the next qres_check reports as QRES_ERR_DEVICE. The kernel returns either way and the context stays
+ * usable. It exercises the lost-peer path on one GPU with a word that nothing advances; it has no counterpart in
+ * the reference, whose device waits have no limit. */
+QRES_API qres_status qres_wait_probe(qres_ctx* ctx, const uint32_t* flag, uint32_t want, uint32_t polls, void* stream);
 /* Kernel launches enqueued by the last qres_decode_step. */
 QRES_API int32_t qres_step_launches(const qres_ctx* ctx);
 

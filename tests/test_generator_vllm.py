@@ -81,3 +81,41 @@ def test_decode_contract():
         a.decode_forward(torch.tensor([[0]]), torch.tensor([0]), reset_batch=True)
     with pytest.raises(AssertionError):
         a.decode_forward(torch.tensor([[0]]), torch.tensor([32]))  # past max_model_len
+
+
+class StandInSpec:
+    """the SpecDecoder surface the MTP block adapter uses"""
+
+    def __init__(self):
+        self.main = SimpleNamespace(vocab=V)
+        self.calls = []
+
+    def start(self, prompt):
+        self.calls.append(("start", list(prompt)))
+        lg = torch.zeros(V)
+        lg[5] = 3.0
+        return lg
+
+    def next_block(self, n, limit):
+        self.calls.append(("block", n, limit))
+        return [1, 2, 3] if limit > 20 else [1]
+
+    def stop(self):
+        self.calls.append(("stop",))
+
+
+def test_mtp_block_adapter_contract():
+    from tt_qwen_resident_b200.generator_vllm import MTP_BLOCK, Qwen36ResidentMTPForCausalLM
+
+    s = StandInSpec()
+    a = Qwen36ResidentMTPForCausalLM(s, max_seq_len=32, eos=9)
+    lg = a.prefill_forward(torch.tensor([[4, 4, 4]]), None, None, torch.tensor([3]))
+    assert s.calls[0] == ("start", [4, 4, 4])
+    assert lg.shape == (1, 1, V) and int(lg.view(-1).argmax()) == 5 and float(lg.view(-1)[0]) == float("-inf")
+    with pytest.raises(RuntimeError):
+        a.decode_forward(torch.tensor([[6]]), torch.tensor([3]))  # not the argmax the device decodes from
+    out = a.decode_forward(torch.tensor([[5]]), torch.tensor([3]))
+    assert out.dtype == torch.int32 and out.shape == (1, MTP_BLOCK)
+    assert out[0].tolist() == [1, 2, 3] + [9] * (MTP_BLOCK - 3)  # short blocks padded with eos
+    a.release_request(0)
+    assert s.calls[-1] == ("stop",)

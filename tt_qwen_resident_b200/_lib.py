@@ -51,6 +51,7 @@ EXPORTS = [
     "qres_replay",
     "qres_release_graph",
     "qres_check",
+    "qres_wait_probe",
     "qres_step_launches",
     "qres_gemv_workspace_size",
     "qres_gemv",
@@ -159,6 +160,7 @@ def lib():
             "qres_replay": [vp, vp],
             "qres_release_graph": [vp],
             "qres_check": [vp, vp],
+            "qres_wait_probe": [vp, vp, ctypes.c_uint32, ctypes.c_uint32, vp],
             "qres_gemv_workspace_size": [i32, i32, ctypes.POINTER(sz)],
             "qres_gemv": [ctypes.POINTER(Weight), i32, i32, vp, i32, vp, i32, vp, vp, sz, vp],
             "qres_gdn_mixer": [i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],

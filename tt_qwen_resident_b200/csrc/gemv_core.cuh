@@ -128,8 +128,6 @@ __device__ __forceinline__ void tmem_load<16>(uint32_t a, float* v) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 // two floats -> two e4m3 bytes (round to nearest even, saturating), a in the low byte
 __device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
     uint16_t r;

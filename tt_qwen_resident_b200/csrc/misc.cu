@@ -413,6 +413,18 @@ cudaError_t kv_rows_launch(uint16_t* kp, uint16_t* vp, uint16_t* k, uint16_t* v,
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------------------------------ wait probe
+// One bounded wait of the peer exchange's kind (wait_count on a counter word) with a caller-chosen budget: the
+// failure path of a lost peer exercised on one GPU, with a word that nothing advances (qres_wait_probe).
+__global__ void wait_probe_kernel(const uint32_t* flag, uint32_t want, uint32_t limit, uint32_t* err) {
+    wait_count(flag, want, err, limit);
+}
+
+cudaError_t wait_probe_launch(const uint32_t* flag, uint32_t want, uint32_t limit, uint32_t* err, cudaStream_t st) {
+    wait_probe_kernel<<<1, 1, 0, st>>>(flag, want, limit, err);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------------ launchers
 static cudaLaunchConfig_t pdl_cfg(dim3 g, dim3 b, size_t smem, cudaStream_t st, cudaLaunchAttribute* at, bool pdl) {
     cudaLaunchConfig_t cfg = {};

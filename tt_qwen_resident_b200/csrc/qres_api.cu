@@ -61,6 +61,7 @@ cudaError_t sample_launch(int rows, const uint32_t* lists, const uint32_t* words
                           cudaStream_t st);
 cudaError_t kv_rows_launch(uint16_t* kp, uint16_t* vp, uint16_t* k, uint16_t* v, const int32_t* page_table, int npos,
                            int nkv, int num_pages, bool to_pages, uint32_t* err, cudaStream_t st);
+cudaError_t wait_probe_launch(const uint32_t* flag, uint32_t want, uint32_t limit, uint32_t* err, cudaStream_t st);
 }  // namespace qres
 
 using namespace qres;
@@ -1000,6 +1001,13 @@ qres_status qres_check(qres_ctx* c, void* stream) {
 }
 
 int32_t qres_step_launches(const qres_ctx* c) { return c ? c->launches : 0; }
+
+qres_status qres_wait_probe(qres_ctx* c, const uint32_t* flag, uint32_t want, uint32_t polls, void* stream) {
+    if (!c || !flag || polls == 0) return fail(c, QRES_ERR_ARG, "qres_wait_probe: bad argument");
+    if (!c->err) return fail(c, QRES_ERR_STATE, "qres_wait_probe before qres_bind_workspace");
+    CU(c, wait_probe_launch(flag, want, polls, c->err, static_cast<cudaStream_t>(stream)));
+    return QRES_OK;
+}
 
 int32_t qres_exchange_mode(const qres_ctx* c) {
     if (!c) return -1;

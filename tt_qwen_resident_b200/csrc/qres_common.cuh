@@ -221,9 +221,10 @@ __device__ __forceinline__ uint4 ld_volatile128(const void* p) {
 // spin budget on a peer counter: ~2^24 polls with a short sleep (about a second), far beyond a healthy step
 constexpr uint32_t kPeerSpinLimit = 1u << 24;
 
-// wait until the counter reaches `want` (wrap-safe compare); false (error bits set) when the budget runs out
-__device__ inline bool wait_count(const uint32_t* p, uint32_t want, uint32_t* err) {
-    for (uint32_t i = 0; i < kPeerSpinLimit; ++i) {
+// wait until the counter reaches `want` (wrap-safe compare); false (error bits set) when the budget of `limit`
+// polls runs out
+__device__ inline bool wait_count(const uint32_t* p, uint32_t want, uint32_t* err, uint32_t limit = kPeerSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if ((int32_t)(ld_acquire_sys(p) - want) >= 0) return true;
         __nanosleep(64);
     }
@@ -290,6 +291,9 @@ __device__ __forceinline__ void l2_prefetch_heads(const L2Heads& h, int i, int n
             bulk_prefetch_l2(h.w + (size_t)(u0 + u) * 16384, (uint32_t)min(4, m - u) * 16384u);
     }
 }
+
+// order this thread's generic-proxy shared-memory accesses before later async-proxy ones (tensor core, bulk copy)
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // named barrier over a subset of warps (id 1.., count a multiple of 32)
 __device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }

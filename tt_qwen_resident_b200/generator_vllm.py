@@ -14,6 +14,8 @@ chunked pipeline-parallel prefill is not part of this build); weights come from 
 ``weights.random_canonical`` or a converted checkpoint) since the reference's Tenstorrent checkpoint loader does
 not apply.
 """
+import os
+
 import torch
 
 from . import weights as W
@@ -134,3 +136,58 @@ class Qwen36ResidentForCausalLM:
         if out.dtype != torch.int32:  # logits of a host-sampled step
             return out
         return out.reshape(-1)[:1].to(torch.int32).view(1, 1).clone()
+
+
+MTP_BLOCK = int(os.environ.get("QWEN36_MTP_BLOCK", "4"))
+
+
+class Qwen36ResidentMTPForCausalLM(Qwen36ResidentForCausalLM):
+    """Greedy MTP speculative decode through the plugin's block output (generator_vllm.py:167-228): every decode
+    step commits MTP_BLOCK tokens (fewer only at the position limit, padded with eos). Greedy only: the device
+    decodes from its own greedy tokens, so the runner's first token (sampled from the prefill's logits) must be
+    their argmax; anything else raises. One user (max_num_seqs=1)."""
+
+    model_capabilities = {
+        "supports_prefix_caching": False,
+        "supports_async_decode": True,
+        "supports_sample_on_device": True,
+        "supports_device_penalties": False,
+        "output_tokens_per_step": MTP_BLOCK,
+        "tt_adaptive_block_output": True,
+    }
+
+    def __init__(self, spec, max_seq_len, eos, mrope=False):
+        self.spec = spec
+        self.vocab = spec.main.vocab
+        self.max_seq_len = max_seq_len
+        self.eos = int(eos)
+        self.mrope = mrope
+        self._first = None
+
+    def prefill_forward(self, tokens, page_table, kv_cache, prompt_lens, **kwargs):
+        assert tokens.shape[0] == 1, "one user per prefill"
+        T = int(prompt_lens[0]) if prompt_lens is not None else tokens.shape[1]
+        logits = self.spec.start(tokens[0, :T].tolist())
+        self._first = int(logits.argmax())
+        # only the argmax the device decodes from may be sampled (the plugin samples block models' prefill
+        # logits at temperature 1)
+        logits = torch.full_like(logits, float("-inf"))
+        logits[self._first] = 0
+        logits = logits.view(1, 1, -1)
+        return (logits, torch.zeros(1, dtype=torch.long)) if self.mrope else logits
+
+    def decode_forward(self, tokens, start_pos, *args, **kwargs):
+        if self._first is not None:
+            token = int(tokens.reshape(-1)[0])
+            if token != self._first:
+                raise RuntimeError(f"MTP serving is greedy only: the runner's first token {token} is not the argmax "
+                                   f"{self._first} the device decodes from")
+            self._first = None
+        block = self.spec.next_block(MTP_BLOCK, self.max_seq_len)
+        out = torch.full((1, MTP_BLOCK), self.eos, dtype=torch.int32)
+        out[0, : len(block)] = torch.tensor(block, dtype=torch.int32)
+        return out
+
+    def release_request(self, row):
+        self.spec.stop()
+        self._first = None
