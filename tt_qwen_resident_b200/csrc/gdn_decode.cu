@@ -59,7 +59,7 @@ struct GdnParams {
     uint32_t* err;
 };
 
-__global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads) gdn_decode_kernel(const GdnParams p) {
+__global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads, 5) gdn_decode_kernel(const GdnParams p) {
     cg::cluster_group cluster = cg::this_cluster();
     const int hh = blockIdx.x;  // local value head
     const int b = blockIdx.y;   // user
@@ -125,6 +125,9 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
         for (int i = 0; i < 8; ++i) s[i] = reinterpret_cast<const float4*>(Sin + (size_t)(rp * 8 + i) * kDV)[cq];
     }
     uint16_t* hist = p.hist + (size_t)(R ? 0 : b) * QRES_HIST_SLOTS * conv;
+    // the head's per-layer parameters (immutable) and this CTA's gated-norm weights, loaded once
+    const float dt_h = p.dt[hh], na_h = p.neg_a[hh];
+    const float nw_c = p.norm_w[c0 + lane];
     for (int row = 0; row < nrows; ++row) {
         const int bb = R ? row : b;  // the row's index in y / o
         const int pos = p0 + (R ? row : 0);
@@ -132,6 +135,12 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
         const YIn y = yall.at((size_t)bb * p.ld_y);
         float* S = p.state + (R ? (size_t)((s0slot + row) % R) * slot_stride : (size_t)b * slot_stride) +
                    (size_t)hh * kDK * kDV + c0;
+        // every in-projection value this row needs besides the conv inputs, issued with them: a, b of the head and
+        // z of this CTA's columns (no load waits behind a barrier later)
+        const int a_off = 2 * gq + 2 * gv;
+        const uint16_t a_raw = bad ? 0 : y[a_off + hh];
+        const uint16_t b_raw = bad ? 0 : y[a_off + p.nv + hh];
+        const uint16_t z_raw = bad ? 0 : y[2 * gq + gv + hh * kDV + c0 + lane];
         if (!bad) {
             const int swr = pos % QRES_HIST_SLOTS;
             // ---- conv1d + SiLU: q, k of the key head (256 channels) and this CTA's 32 v channels; a thread's
@@ -202,9 +211,8 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
                 if (which == 0) qs[e] = mul_rn(v, 0.08838834764831845f);
                 else ks[e] = v;
             }
-            const int a_off = 2 * gq + 2 * gv;
-            const float av = __uint_as_float((uint32_t)y[a_off + hh] << 16);
-            decay = expf(mul_rn(p.neg_a[hh], softplus_f(add_rn(av, p.dt[hh]))));
+            const float av = __uint_as_float((uint32_t)a_raw << 16);
+            decay = expf(mul_rn(na_h, softplus_f(add_rn(av, dt_h))));
         }
         __syncthreads();
         float part[4] = {0.f, 0.f, 0.f, 0.f};
@@ -223,8 +231,7 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
         }
         __syncthreads();
         if (!bad && tid < kGdnCols) {
-            const float bv = __uint_as_float((uint32_t)y[2 * gq + 2 * gv + p.nv + hh] << 16);
-            const float beta = sigmoid_f(bv);
+            const float beta = sigmoid_f(__uint_as_float((uint32_t)b_raw << 16));
             float t = 0.f;
 #pragma unroll
             for (int w = 0; w < 16; ++w) t += red[w][tid];
@@ -274,8 +281,8 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads)
             const float mean = tot / (float)kDV;
             const float rr = rsqrt_ieee(mean + kEps);
             const int col = c0 + lane;
-            const float on = mul_rn(mul_rn(ov, rr), p.norm_w[col]);
-            const float z = __uint_as_float((uint32_t)y[2 * gq + gv + hh * kDV + col] << 16);
+            const float on = mul_rn(mul_rn(ov, rr), nw_c);
+            const float z = __uint_as_float((uint32_t)z_raw << 16);
             const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(on, silu_f(z)));
             const size_t idx = (size_t)bb * gv + hh * kDV + col;
             reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
