@@ -392,26 +392,29 @@ def e2e_run(model, args, batch, stream, world, dev):
     return ms, _lib.TOK_WORDS * 4, batch * 16
 
 
-def gateup_alone(model, rows, stream, dev):
-    """the dominant kernel, the gate|up GEMV (rmsnorm prologue + SwiGLU epilogue), timed alone with CUDA events on
-    its stream: layers 0 and 1 alternate, so every launch streams weights that are not in L2 (2 x 178 MB > 126 MB).
-    Returns (ms per launch, algorithmic bytes per launch)."""
+def gateup_alone(model, rows, stream, dev, epi=1):
+    """the dominant kernel, the gate|up GEMV (rmsnorm prologue; epi 1: SwiGLU epilogue, 4: the step's fixed-point
+    accumulators), timed alone with CUDA events on its stream: layers 0 and 1 alternate, so every launch streams
+    weights that are not in L2 (2 x 178 MB > 126 MB). Returns (ms per launch, algorithmic bytes per launch)."""
     from tt_qwen_resident_b200 import _lib
 
     gws = model.w_gu[:2] if len(model.w_gu) > 1 else model.w_gu[:1]
     xin = torch.randn(rows, 5120, device=dev)
-    aout = torch.empty(rows, model.d.ic, dtype=torch.bfloat16, device=dev)
+    if epi == 4:
+        aout = torch.zeros(rows, 2 * model.d.ic, dtype=torch.int64, device=dev)
+    else:
+        aout = torch.empty(rows, model.d.ic, dtype=torch.bfloat16, device=dev)
     flush = None if len(gws) > 1 else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     with torch.cuda.stream(stream):
         for k in range(4):
-            _lib.gemv(gws[k % len(gws)], xin, 0, 1, aout, stream=stream)
+            _lib.gemv(gws[k % len(gws)], xin, 0, epi, aout, stream=stream)
         ts = []
         for k in range(20):
             if flush is not None:
                 flush.zero_()  # one layer only: evict L2 between launches
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            _lib.gemv(gws[k % len(gws)], xin, 0, 1, aout, stream=stream)
+            _lib.gemv(gws[k % len(gws)], xin, 0, epi, aout, stream=stream)
             b.record(stream)
             ts.append((a, b))
     stream.synchronize()
@@ -455,7 +458,9 @@ def run_ours(args, rank, world, local):
     ms, clocks, end_pos = decode_run(model, args, batch, prompt, stream, world, dev, local, pos0=args.ctx)
     launches_per_step = model.launches
     e2e_ms, h2d, d2h = e2e_run(model, args, batch, stream, world, dev)
-    gemv_ms, gemv_bytes = gateup_alone(model, batch, stream, dev)
+    # at 4 or more rows the step's accumulating form walks K groups: time that form
+    gemv_ms, gemv_bytes = gateup_alone(model, batch, stream, dev,
+                                       epi=4 if batch >= 4 and model.exchange in ("none", "counted") else 1)
     peak, peak_kind = peaks()
     gemv_gbs = gemv_bytes / (gemv_ms * 1e-3) / 1e9
     step_bytes = model.weight_bytes + model.state_bytes_per_step(ctx=end_pos - args.steps // 2)
@@ -469,12 +474,13 @@ def run_ours(args, rank, world, local):
                            p2p=world > 1 and args.exchange == "p2p", device=dev, share=model)
         m8.capture_trace(stream)
         ms8, clocks8, end8 = decode_run(m8, args, 8, 128, stream, world, dev, local)
-        g8_ms, g8_bytes = gateup_alone(m8, 8, stream, dev)
+        g8_ms, g8_bytes = gateup_alone(m8, 8, stream, dev, epi=4 if m8.exchange in ("none", "counted") else 1)
         sb8 = m8.weight_bytes + m8.state_bytes_per_step(ctx=end8 - args.steps // 2)
         b8 = {
             "metric": metric_name(8), "value": 8e3 / ms8, "unit": "tok/s", "ms_per_step": ms8,
             "workload": "config4: 8 users, 128-token uniform-random prompts each, greedy decode",
             "exchange": m8.exchange, "launches_per_step": m8.launches, "clocks": clocks8,
+            "split_tiles": "fixed-point accumulators" if m8.exchange in ("none", "counted") else "finished by ticket",
             "step_roofline": {"bytes_per_step_per_gpu": sb8, "achieved_GBps": sb8 / (ms8 * 1e-3) / 1e9,
                               "frac": sb8 / (ms8 * 1e-3) / 1e9 / peak},
             "gateup_8rows": {"ms_per_launch": g8_ms, "achieved_GBps": g8_bytes / (g8_ms * 1e-3) / 1e9,
@@ -487,7 +493,7 @@ def run_ours(args, rank, world, local):
         e2e_v = batch * 1e3 / e2e_ms if batch > 1 else 1e3 / e2e_ms
         cfg = config_of(args, world)
         cfg.update({
-            "split_tiles": "fixed-point accumulators" if exchange in ("none", "counted") and batch <= 2 and not args.tile_finish
+            "split_tiles": "fixed-point accumulators" if exchange in ("none", "counted") and not args.tile_finish
             else "finished by ticket",
             "exchange": {"none": None, "counted": "counted fixed-point words over NVLink (GEMV epilogue)",
                          "tagged": "tagged words over NVLink (GEMV epilogue)", "nccl": "NCCL"}[exchange],

@@ -73,7 +73,7 @@ typedef struct {
  * continuing after accepting row k uses position p + k + 1 and slot (tok.slot + k) % rows (no rollback). The
  * conv history and the KV cache are position-keyed and need nothing. */
 #define QRES_FLAG_VERIFY 1
-/* qres_config.flags: with an lm_head and up to 2 rows (one rank, or ranks with the peer window of qres_p2p_open
+/* qres_config.flags: with an lm_head (one rank, or ranks with the peer window of qres_p2p_open
  * and native peer atomics), the in-, out-, gate|up and down-projections add each CTA's partial sums into 64-bit
  * fixed-point accumulators (2^-30 units) with one atomic add per row, and the consumer reads the sums: the next
  * prologue (the residual add, or silu(g) * u) or the mixer (rounding them to bf16). The row-parallel out- and
@@ -239,7 +239,9 @@ QRES_API int32_t qres_step_launches(const qres_ctx* ctx);
 /* ---- single kernels (the building blocks of a step, for tests and microbenchmarks) ---- */
 /* y = act(h @ W^T) for `rows` users: pro 0 = h = bf16(rmsnorm(x)) from fp32 x [rows][K]; pro 1 = h = bf16
  * input [rows][K]. epi 0 = bf16 out [rows][w.rows]; 1 = SwiGLU over interleaved gate|up pairs, bf16 out
- * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc. grid: CTAs requested (0 = twice
+ * [rows][w.rows / 2]; 2 = fp32 out[r] += acc (residual); 3 = fp32 out = acc; 4 = the step's fixed-point
+ * accumulation: out int64 [rows][w.rows] += round(acc * 2^30) with one atomic add per CTA and row (out zeroed by
+ * the caller; value = out * 2^-30; with 4 or more rows the units are walked in K groups as in the step). grid: CTAs requested (0 = twice
  * the SM count; fewer are launched when the weight has fewer 128 x 128 units). work: qres_gemv_workspace_size
  * bytes for that grid (split-tile tickets and partials), zeroed once before first use (every launch leaves it
  * reusable). */

@@ -8,7 +8,8 @@ CTAs' atomic adds interleave: eager and CUDA-graph replays of the same inputs ag
 round differently (one float rounding of the exact sum of 2^-30-rounded parts, against fp32 additions in CTA
 order); a flipped bf16 rounding of an activation carries on through the recurrent state, so by the third step
 the two agree to ~5e-3 relative (asserted: 1e-2), and each stays within test_model_gpu's 2e-2 of the oracle at
-every one of three consecutive steps of the G G G A x2 + lm_head schedule, at 1 and 2 rows."""
+every one of three consecutive steps of the G G G A x2 + lm_head schedule, at 1, 2 and 8 rows (at 8 rows the
+accumulating projections walk their units in K groups, several CTAs adding into every tile)."""
 import pytest
 import torch
 
@@ -20,7 +21,7 @@ from test_model_gpu import rel, setup8  # noqa: F401
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("rows", [1, 2])
+@pytest.mark.parametrize("rows", [1, 2, 8])
 def test_accumulators_match_tile_finish_and_oracle(cuda, setup8, rows):
     w8, P = setup8
     layers, interval, pos = 8, 4, 100

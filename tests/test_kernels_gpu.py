@@ -106,6 +106,15 @@ def test_gemv_parity(cuda, rows, N, K):
     ref2 = hb @ wd.T + resid
     rel = float((o2.cpu() - ref2).norm() / ref2.norm())
     assert rel < 1e-5, rel
+    # the step's fixed-point accumulation (epi 4; with 4 or more rows the units walk in K groups): value = out 2^-30
+    acc = torch.zeros(rows, N, dtype=torch.int64, device=cuda)
+    _lib.gemv(gw, hb_d, 1, 4, acc, err)
+    got = acc.cpu().double() * 2.0**-30
+    ref3 = hb.double() @ wd.T.double()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    rel = float((got - ref3).norm() / ref3.norm())
+    assert rel < 1e-5, rel
 
 
 @pytest.mark.parametrize("rows", [1, 5])

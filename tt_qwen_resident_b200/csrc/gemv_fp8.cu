@@ -64,6 +64,7 @@ struct GemvParams {
     int ld_out;
     int nstages;            // ring depth
     int nkw;                // K blocks in this CTA's activation window (the most any CTA needs)
+    int nq;                 // unit order: K blocks per group (nkb = storage order; see unit_offset)
     float* part;            // [grid][2][8][128]: a CTA's split first / last tile
     int* ticket;            // [tiles]
     L2Heads next;           // the next projection of the step: the heads of its CTA runs are pulled into L2
@@ -81,6 +82,28 @@ struct GemvParams {
     // contributions per word; the producer split its units as base rc_base, remainder rc_rem, rc_nkb per tile
     int rc_ranks, rc_base, rc_rem, rc_nkb;
     uint32_t* err;
+};
+
+// walks a CTA's run of units in the launch's unit order: (K group, tile, K block in the group)
+struct UnitWalk {
+    int tiles, nq, kq, T, kbi;
+    __device__ UnitWalk(int u, int tiles_, int nq_) : tiles(tiles_), nq(nq_) {
+        const int per = tiles * nq;
+        kq = u / per;
+        const int r = u - kq * per;
+        T = r / nq;
+        kbi = r - T * nq;
+    }
+    __device__ int kb() const { return kq * nq + kbi; }
+    __device__ void next() {
+        if (++kbi == nq) {
+            kbi = 0;
+            if (++T == tiles) {
+                T = 0;
+                ++kq;
+            }
+        }
+    }
 };
 
 template <int B, int PRO, int EPI>
@@ -111,8 +134,18 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     const int cnt = base + ((int)blockIdx.x < rem ? 1 : 0);
     const int NS = p.nstages;
     if (cnt == 0) return;
-    const int kb_start = u0 % nkb;
-    const int nwin = min(cnt, nkb);  // K blocks this CTA touches: a cyclic run starting at kb_start
+    // the K blocks this CTA touches (its activation window): in storage order (nq = nkb) a cyclic run from its
+    // first unit's block; in grouped order the K groups its run spans
+    const int nq = p.nq;
+    int kb_start, nwin;
+    if (nq == nkb) {
+        kb_start = u0 % nkb;
+        nwin = min(cnt, nkb);
+    } else {
+        const int per = p.tiles * nq, kq0 = u0 / per, kq1 = (u0 + cnt - 1) / per;
+        kb_start = kq0 * nq;
+        nwin = min((kq1 - kq0 + 1) * nq, nkb);
+    }
 
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
@@ -136,7 +169,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     auto issue = [&](int i) {
         const int slot = i % NS;
         mbar_arrive_expect_tx(&full[slot], kUnitBytes);
-        bulk_g2s_hint(ring + (size_t)slot * kUnitBytes, p.w + (size_t)(u0 + i) * kUnitBytes, kUnitBytes, &full[slot], pol);
+        bulk_g2s_hint(ring + (size_t)slot * kUnitBytes, p.w + unit_offset(u0 + i, p.tiles, nkb, nq) * kUnitBytes,
+                      kUnitBytes, &full[slot], pol);
     };
     if (tid == 0)
         for (int i = 0; i < min(NS, cnt); ++i) issue(i);
@@ -278,7 +312,40 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     constexpr int kXj = 8;
     const bool regs = kRegs && K <= kXj * 4 * kGemvThreads && p.seg == 0;
     float rn[B], rn2[B];  // rn2: the second segment's (two-segment prologue)
-    if (PRO == PRO_RMSNORM || kAdd) {
+    if ((PRO == PRO_RMSNORM || kAdd) && !kRegs && p.seg == 0) {
+        // more than 2 rows: the sums of squares with two users' loads in flight together (x_out by CTA 0)
+#pragma unroll
+        for (int b0 = 0; b0 < B; b0 += 2) {
+            float ssa = 0.f, ssb = 0.f;
+#pragma unroll 5
+            for (int i = tid; i < K / 4; i += kGemvThreads) {
+                float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+                if (b0 < users) va = xload(b0, i);
+                if (b0 + 1 < users) vb = xload(b0 + 1, i);
+                if (kAdd && blockIdx.x == 0) {
+                    if (b0 < users) reinterpret_cast<float4*>(p.x_out + (size_t)b0 * K)[i] = va;
+                    if (b0 + 1 < users) reinterpret_cast<float4*>(p.x_out + (size_t)(b0 + 1) * K)[i] = vb;
+                }
+                ssa += va.x * va.x + va.y * va.y + va.z * va.z + va.w * va.w;
+                ssb += vb.x * vb.x + vb.y * vb.y + vb.z * vb.z + vb.w * vb.w;
+            }
+            ssa = warp_sum(ssa);
+            ssb = warp_sum(ssb);
+            if (lane == 0) {
+                red[warp][b0] = ssa;
+                if (b0 + 1 < B) red[warp][b0 + 1] = ssb;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            float tsum = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) tsum += red[w][b];
+            rn[b] = rsqrt_ieee(tsum / (float)K + kEps);
+            rn2[b] = rn[b];
+        }
+    } else if (PRO == PRO_RMSNORM || kAdd) {
         float4 xr[kRegs ? B : 1][kXj];
 #pragma unroll
         for (int b = 0; b < B; ++b) {
@@ -441,9 +508,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         if (lane == 0) {
             const uint32_t ring_a = smem_addr(ring), act_a = smem_addr(act);
             const uint32_t sbo_b = B > 4 ? (uint32_t)gstride : 0u;  // users 4..7 (columns 8..15)
-            int ws = 0;
+            UnitWalk it(u0, p.tiles, nq);
             for (int i = 0; i < cnt; ++i) {
                 const int slot = i % NS, d = i % kDSlots;
+                int ws = it.kb() - kb_start;
+                if (ws < 0) ws += nkb;
+                it.next();
                 if (!mbar_wait(&full[slot], (i / NS) & 1, p.err)) break;
                 if (i >= kDSlots && !mbar_wait(&dempty[d], ((i / kDSlots) - 1) & 1, p.err)) break;
                 tc_fence_after();
@@ -455,7 +525,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
                 }
                 tc_commit(&empty[slot]);
                 tc_commit(&dfull[d]);
-                if (++ws == nkb) ws = 0;
             }
             tc_commit(drain);
             mbar_wait(drain, 0, p.err);
@@ -591,21 +660,20 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         };
 
         // the scale of the next unit is loaded one unit ahead
-        int T = u0 / nkb, kb = kb_start, ws = 0;
-        int sel = p.table[(size_t)T * tstride + row];
-        float s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)T * tstride + kSelBytes) + kb * 8 + sel);
+        UnitWalk it(u0, p.tiles, nq);
+        int sel = p.table[(size_t)it.T * tstride + row];
+        float s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)it.T * tstride + kSelBytes) + it.kb() * 8 + sel);
         const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
         for (int i = 0; i < cnt; ++i) {
             const float s = s_next;
-            const int Tc = T, wsc = ws;
-            if (++kb == nkb) {
-                kb = 0;
-                ++T;
-                if (i + 1 < cnt) sel = p.table[(size_t)T * tstride + row];
+            const int Tc = it.T;
+            int wsc = it.kb() - kb_start;
+            if (wsc < 0) wsc += nkb;
+            it.next();
+            if (i + 1 < cnt) {
+                if (it.T != Tc) sel = p.table[(size_t)it.T * tstride + row];
+                s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)it.T * tstride + kSelBytes) + it.kb() * 8 + sel);
             }
-            if (++ws == nkb) ws = 0;
-            if (i + 1 < cnt)
-                s_next = __ldg(reinterpret_cast<const float*>(p.table + (size_t)T * tstride + kSelBytes) + kb * 8 + sel);
             // after a timeout the warp keeps its place in the loop without waiting (its results are void, the
             // error word is set): every epilogue warp reaches the same tile flushes and their named barriers
             const int d = i % kDSlots;
@@ -709,6 +777,20 @@ constexpr int kMinStages = 3;
 
 static int bt_of(int users) { return users == 1 ? 1 : users == 2 ? 2 : users <= 4 ? 4 : 8; }
 
+// K blocks per group of the launch's unit order (unit_offset): the plain fixed-point accumulators (EPI_ACC) take
+// any number of partial sums per tile, so with 4 or more rows -- whose hi / lo operand costs 1 or 2 KB of shared
+// memory per K block -- a CTA's run covers a few tiles of one K group (at most ~12 KB of operand per group)
+// instead of one tile's whole K: a small activation window leaves room for a deep ring and two CTAs per SM and
+// builds fewer operand blocks. Every other launch walks the storage order (nkb).
+int gemv_group_blocks(int users, int epi, int K) {
+    const int nkb = K / 128, Bt = bt_of(users);
+    if (epi != EPI_ACC || Bt < 4) return nkb;
+    const int per_kb = 8 * gemv_act_lbo(Bt) * (Bt > 4 ? 2 : 1) + 32;
+    for (int d = nkb; d >= 2; --d)
+        if (nkb % d == 0 && d * per_kb <= 12 * 1024) return d;
+    return nkb;
+}
+
 // workspace: the tile tickets at a fixed place (they must read zero at every launch, whatever the grid or the
 // weight: each launch leaves the ones it used at zero), then a [grid][2][8][128] fp32 part buffer per launch
 constexpr int kGemvMaxTiles = 4096;  // 524,288 rows
@@ -810,12 +892,23 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
     p.out = out;
     p.ld_out = ld_out;
     p.err = err;
-    p.next = next ? *next : L2Heads{nullptr, 0, 0, 0, 0};
+    p.next = next ? *next : L2Heads{nullptr, 0, 0, 0, 0, 1, 1, 1};
     uint8_t* wk = static_cast<uint8_t*>(work);
     p.ticket = reinterpret_cast<int*>(wk);
     p.part = reinterpret_cast<float*>(wk + (size_t)kGemvMaxTiles * 4);
     const int U = tiles * nkb;
-    p.nkw = std::min((U + grid - 1) / grid, nkb);
+    p.nq = gemv_group_blocks(users, epi, w.K);
+    if (p.nq == nkb) {
+        p.nkw = std::min((U + grid - 1) / grid, nkb);
+    } else {
+        // the widest window: the K groups a CTA's run spans
+        const int b = U / grid, r = U % grid, per = tiles * p.nq;
+        p.nkw = 0;
+        for (int c = 0; c < grid; ++c) {
+            const int u0 = c * b + std::min(c, r), cnt = b + (c < r ? 1 : 0);
+            p.nkw = std::max(p.nkw, std::min(((u0 + cnt - 1) / per - u0 / per + 1) * p.nq, nkb));
+        }
+    }
     // ring depth: as deep as half an SM allows, else as deep as the per-CTA maximum allows
     const size_t fixed = gemv_smem_bytes(Bt, p.nkw, 0);
     int ns = fixed < kGemvSmemBudget ? (int)((kGemvSmemBudget - fixed) / kUnitBytes) : 0;

@@ -28,6 +28,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
                         void* work, size_t work_bytes, const L2Heads* next, const GemvExchange* ex = nullptr);
 size_t gemv_workspace_bytes(int grid);
 int gemv_grid(int users, int rows_pad, int K, int grid);
+int gemv_group_blocks(int users, int epi, int K);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -608,11 +609,11 @@ qres_status qres_nccl_init(qres_ctx* c, const char* libpath, const void* id128) 
     return QRES_OK;
 }
 
-// the fixed-point accumulators (EPI_ACC; between ranks the counted exchange): with an lm_head, up to 2 rows, not
+// the fixed-point accumulators (EPI_ACC; between ranks the counted exchange): with an lm_head, any row count, not
 // switched off by QRES_FLAG_TILE_FINISH, and across ranks only over the peer window with native peer atomics
 static bool uses_accumulators(const qres_ctx* c) {
     const bool tp = c->nranks > 1;
-    return !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 && c->cfg.rows <= 2 &&
+    return !(c->cfg.flags & QRES_FLAG_TILE_FINISH) && c->cfg.vocab > 0 &&
            (!tp || (c->p2p_on && c->p2p_atomics));
 }
 
@@ -679,9 +680,13 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     }
     if (c->cfg.vocab) order.push_back(&c->head);
     // units k0 .. k0 + k - 1 of every CTA run of projection w as that launch will split it
+    const bool accm = uses_accumulators(c);
     auto heads_of = [&](const qres_weight& w, int k0, int k) -> L2Heads {
         const int units = (w.rows_pad / 128) * (w.K / 128);
-        return L2Heads{static_cast<const uint8_t*>(w.data), units, gemv_grid(R, w.rows_pad, w.K, grid_of(w)), k0, k};
+        // the unit order of that launch: grouped only for the accumulating projections (not the lm_head)
+        const int nq = gemv_group_blocks(R, (accm && &w != &c->head) ? EPI_ACC : EPI_BF16, w.K);
+        return L2Heads{static_cast<const uint8_t*>(w.data), units, gemv_grid(R, w.rows_pad, w.K, grid_of(w)), k0, k,
+                       w.rows_pad / 128, w.K / 128, nq};
     };
     // (deeper prefetch, here or from the mixers, measured slower: it competes with the stream it precedes)
     const int kPrefetchUnits = 2;  // 32 KB per CTA run
@@ -698,7 +703,7 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                              c->gemv_work_bytes, next_of(&w)),
                  what);
     };
-    // Fixed-point accumulators (EPI_ACC, up to 2 rows, with an lm_head; over ranks with the peer exchange and native
+    // Fixed-point accumulators (EPI_ACC, with an lm_head; over ranks with the peer exchange and native
     // peer atomics). The in-projection and gate|up add into this rank's buffers (accD, read by the mixer; accB,
     // read by the down prologue as silu(g) * u). The row-parallel out- and down-projections add into XA and XC,
     // which the next rmsnorm prologue adds to the residual. Each launch zeroes a buffer whose last reader finished
@@ -709,7 +714,6 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
     //   XA / XC (in the peer window), and the next prologue reads them once each word holds all contributions.
     //   In-proj zeroes accB, out-proj XC, gate|up accD, down XA -- the exchange buffers with a system-scope fence:
     //   peers add into them only after this rank's next contributions, which follow the fence.
-    const bool accm = uses_accumulators(c);
     long long* const accB = c->acc[1];
     long long* const accD = c->acc[3];
     long long* xa_at[8] = {};
@@ -1033,7 +1037,7 @@ qres_status qres_gemv_workspace_size(int32_t grid, int32_t rows_pad, size_t* byt
 
 qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const void* in, int32_t epi, void* out,
                       int32_t grid, uint32_t* err, void* work, size_t work_bytes, void* stream) {
-    if (!w || !in || !out || !work || pro < 0 || pro > 1 || epi < 0 || epi > 3)
+    if (!w || !in || !out || !work || pro < 0 || pro > 1 || epi < 0 || epi > 4)
         return fail(nullptr, QRES_ERR_ARG, "qres_gemv: bad argument");
     if (grid <= 0) {
         int dev = 0;
@@ -1042,8 +1046,11 @@ qres_status qres_gemv(const qres_weight* w, int32_t rows, int32_t pro, const voi
         grid *= 2;  // two CTAs per SM
     }
     const int ld_out = epi == 1 ? w->rows / 2 : w->rows;
-    cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, epi, out, ld_out, grid, err, static_cast<cudaStream_t>(stream),
-                                 false, nullptr, nullptr, work, work_bytes, nullptr);
+    GemvExchange ex;
+    if (epi == 4) ex.acc_out = static_cast<long long*>(out);  // the step's accumulators (EPI_ACC)
+    cudaError_t ce = gemv_launch(*w, rows, pro, in, w->K, epi == 4 ? EPI_ACC : epi, epi == 4 ? nullptr : out, ld_out, grid,
+                                 err, static_cast<cudaStream_t>(stream), false, nullptr, nullptr, work, work_bytes,
+                                 nullptr, &ex);
     if (ce != cudaSuccess) return fail(nullptr, QRES_ERR_CUDA, "qres_gemv: %s", cudaGetErrorString(ce));
     return QRES_OK;
 }

@@ -278,7 +278,18 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 struct L2Heads {
     const uint8_t* w;
     int units, grid, k0, k;
+    int tiles, nkb, nq;  // the launch's unit order (see unit_offset)
 };
+
+// The order in which a weight-streaming launch walks its units (128-row x 128-K blocks of 16 KB; the weight is
+// stored tile-major, K fastest): units are grouped by K block group (nq blocks each), then tile, then block in the
+// group, and a launch splits that order over its CTAs in contiguous runs. nq = nkb is the plain storage order (a
+// CTA's run covers about one tile's whole K); a smaller nq makes a run cover a few tiles of one K group, so the
+// CTA needs the activations of nq K blocks only. Returns the unit's index in storage order.
+__device__ __forceinline__ size_t unit_offset(int u, int tiles, int nkb, int nq) {
+    const int per = tiles * nq, kq = u / per, r = u - kq * per, T = r / nq;
+    return (size_t)T * nkb + kq * nq + (r - T * nq);
+}
 
 // prefetcher i of n takes the runs i, i + n, ...
 __device__ __forceinline__ void l2_prefetch_heads(const L2Heads& h, int i, int n) {
@@ -287,8 +298,8 @@ __device__ __forceinline__ void l2_prefetch_heads(const L2Heads& h, int i, int n
     for (int c = i; c < h.grid; c += n) {
         const int u0 = c * base + min(c, rem), cnt = base + (c < rem ? 1 : 0);
         const int m = min(cnt, h.k0 + h.k);
-        for (int u = h.k0; u < m; u += 4)
-            bulk_prefetch_l2(h.w + (size_t)(u0 + u) * 16384, (uint32_t)min(4, m - u) * 16384u);
+        for (int u = h.k0; u < m; ++u)
+            bulk_prefetch_l2(h.w + unit_offset(u0 + u, h.tiles, h.nkb, h.nq) * 16384, 16384u);
     }
 }
 

@@ -1,6 +1,6 @@
 """Kernel microbenchmarks of libqres (one kernel at a time, CUDA events, L2 flushed between launches).
 
-  python -m tt_qwen_resident_b200.microbench gemv [--rows 1] [--n 34816] [--k 5120] [--pro 0] [--epi 1]
+  python -m tt_qwen_resident_b200.microbench gemv [--rows 1] [--n 34816] [--k 5120] [--pro 0] [--epi 1]  (epi 4: fixed-point accumulators)
   python -m tt_qwen_resident_b200.microbench gdn [--rows 1] [--tp 1]
   python -m tt_qwen_resident_b200.microbench attn [--rows 1] [--tp 1] [--ctx 4096]
 
@@ -61,6 +61,8 @@ def bench_gemv(a):
         out = torch.empty(a.rows, N // 2, dtype=torch.bfloat16, device=dev)
     elif a.epi == 0:
         out = torch.empty(a.rows, N, dtype=torch.bfloat16, device=dev)
+    elif a.epi == 4:  # the step's fixed-point accumulators (int64; the sums grow over the repetitions)
+        out = torch.zeros(a.rows, N, dtype=torch.int64, device=dev)
     else:
         out = torch.zeros(a.rows, N, device=dev)
     work = _lib.gemv_work(dev, gw.rows_pad, a.grid)

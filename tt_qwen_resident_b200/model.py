@@ -92,7 +92,7 @@ class ResidentModel:
         self.state_copies = (max(gc, 1) if self.n_gdn else 0, max(ac, 1) if self.n_attn else 0)
         L = _lib.lib()
         # tile_finish: split projection tiles finished by their last CTA (ticket) rather than summed in the
-        # fixed-point accumulators the library uses at one rank with up to 2 rows
+        # fixed-point accumulators the library uses by default (with an lm_head)
         flags = (
             (_lib.QRES_FLAG_VERIFY if self.verify else 0)
             | (_lib.QRES_FLAG_TILE_FINISH if tile_finish else 0)
