@@ -425,7 +425,7 @@ def gateup_alone(model, rows, stream, dev, epi=1):
 # (profiles/gemv_fp8_gateup_34816x5120_b1.md; profiles/gemv_fp8_gateup_34816x5120_b8.md: 8 rows, with the tensor
 # pipe's share of the active cycles)
 NCU_GATEUP = {1: dict(traffic=182731008, src="profiles/gemv_fp8_gateup_34816x5120_b1.md"),
-              8: dict(traffic=None, tensor_pipe=None, src="profiles/gemv_fp8_gateup_34816x5120_b8.md")}
+              8: dict(traffic=184298752, tensor_pipe=0.0252, src="profiles/gemv_fp8_gateup_34816x5120_b8.md")}
 
 
 def run_ours(args, rank, world, local):
@@ -485,6 +485,7 @@ def run_ours(args, rank, world, local):
                               "frac": sb8 / (ms8 * 1e-3) / 1e9 / peak},
             "gateup_8rows": {"ms_per_launch": g8_ms, "achieved_GBps": g8_bytes / (g8_ms * 1e-3) / 1e9,
                              "frac": g8_bytes / (g8_ms * 1e-3) / 1e9 / peak,
+                             "traffic": NCU_GATEUP[8]["traffic"], "bytes_per_launch": g8_bytes,
                              "tensor_pipe_active": NCU_GATEUP[8]["tensor_pipe"], "ncu": NCU_GATEUP[8]["src"]},
         }
         m8.close()

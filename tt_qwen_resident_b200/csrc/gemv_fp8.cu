@@ -765,6 +765,72 @@ static cudaError_t launch_pe(const GemvParams& p, int Bt, int grid, size_t smem,
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// The rmsnorm input of a projection formed once per user (the step at 4 or more rows on one rank): x_out = x +
+// the previous projection's fixed-point sums (or x alone), h = bf16(x_out * rsqrt(mean(x_out^2) + eps)). The
+// projection then reads its activation window of h (PRO_BF16) instead of every CTA forming all of x_out and its
+// norm for every user again (at 8 rows that is ~480 KB of reads per CTA before its first MMA). One CTA per user,
+// 640 threads x 8 consecutive elements.
+constexpr int kResidThreads = kHidden / 8;
+
+__global__ void __launch_bounds__(kResidThreads) resid_norm_kernel(const float* x, const long long* racc, float* x_out,
+                                                                    uint16_t* h) {
+    const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float red[kResidThreads / 32];
+    pdl_launch();
+    pdl_wait();
+    const float4* xs = reinterpret_cast<const float4*>(x + (size_t)b * kHidden) + 2 * tid;
+    float v[8];
+    const float4 a0 = xs[0], a1 = xs[1];
+    v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+    v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+    if (racc != nullptr) {
+        const longlong2* ra = reinterpret_cast<const longlong2*>(racc + (size_t)b * kHidden) + 4 * tid;
+        longlong2 q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = __ldcg(ra + j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[2 * j] += acc_decode(q[j].x);
+            v[2 * j + 1] += acc_decode(q[j].y);
+        }
+        float4* xo = reinterpret_cast<float4*>(x_out + (size_t)b * kHidden) + 2 * tid;
+        xo[0] = make_float4(v[0], v[1], v[2], v[3]);
+        xo[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kResidThreads / 32; ++w) t += red[w];
+    const float r = rsqrt_ieee(t / (float)kHidden + kEps);
+    uint32_t hw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        hw[j] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * j] * r)) |
+                ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * j + 1] * r)) << 16);
+    reinterpret_cast<uint4*>(h + (size_t)b * kHidden)[tid] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, float* x_out, uint16_t* h,
+                              cudaStream_t st, bool pdl) {
+    if (users < 1 || users > kMaxRows || (racc && !x_out)) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(users);
+    cfg.blockDim = dim3(kResidThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, resid_norm_kernel, x, racc, x_out, h);
+}
+
 // shared memory of one GEMV CTA: half an SM's (a second CTA -- the next projection's, under programmatic
 // dependent launch -- fits beside it and starts its weight stream during this one's tail); past that, up to
 // the per-CTA maximum with a shallower ring

@@ -29,6 +29,8 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
 size_t gemv_workspace_bytes(int grid);
 int gemv_grid(int users, int rows_pad, int K, int grid);
 int gemv_group_blocks(int users, int epi, int K);
+cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, float* x_out, uint16_t* h,
+                              cudaStream_t st, bool pdl);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -161,6 +163,7 @@ struct qres_ctx {
     uint32_t* err = nullptr;
     float *xb = nullptr, *xe = nullptr, *partial = nullptr;
     uint16_t *y = nullptr, *o = nullptr, *a = nullptr;
+    uint16_t* hbuf = nullptr;  // [rows][5120] bf16: a projection's rmsnorm input formed once (resid_norm)
     int32_t* argmax = nullptr;
     uint32_t* gathered = nullptr;
     void* attn_work = nullptr;
@@ -218,7 +221,7 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // workspace layout: offsets of each scratch region
 struct Carve {
-    size_t err, epoch, xb, xe, partial, y, o, a, argmax, gathered, attn, topk, gemv, gemv_bytes, acc[4], total;
+    size_t err, epoch, xb, xe, partial, y, o, a, hbuf, argmax, gathered, attn, topk, gemv, gemv_bytes, acc[4], total;
 };
 
 Carve carve(const qres_ctx* c) {
@@ -238,6 +241,7 @@ Carve carve(const qres_ctx* c) {
     k.y = take((size_t)R * c->ld_y * 2);
     k.o = take((size_t)R * c->gv * 2);
     k.a = take((size_t)R * c->ic * 2);
+    k.hbuf = take((size_t)R * kHidden * 2);
     k.argmax = take((size_t)R * 4);
     k.gathered = take((size_t)c->nranks * R * 2 * QRES_TOPK * 4);
     k.attn = take(attn_workspace_bytes(c->nranks, R, c->attn_chunks));
@@ -517,6 +521,7 @@ qres_status qres_bind_workspace(qres_ctx* c, void* dev, size_t bytes) {
     c->y = reinterpret_cast<uint16_t*>(w + k.y);
     c->o = reinterpret_cast<uint16_t*>(w + k.o);
     c->a = reinterpret_cast<uint16_t*>(w + k.a);
+    c->hbuf = reinterpret_cast<uint16_t*>(w + k.hbuf);
     c->argmax = reinterpret_cast<int32_t*>(w + k.argmax);
     c->gathered = reinterpret_cast<uint32_t*>(w + k.gathered);
     c->attn_work = w + k.attn;
@@ -744,7 +749,25 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         ex.rc_nkb = pending_acc.nkb;
         pending_acc = Pending();
     };
+    // One rank at 4 or more rows: a projection's rmsnorm input is formed once per user (resid_norm: x + the pending
+    // sums -> the other residual buffer, h = bf16(rmsnorm) -> hbuf) and the projection reads its window of h,
+    // instead of each of its CTAs re-reading every user's residual and sums (~480 KB per CTA at 8 rows).
+    const bool split = accm && !tp && R >= 4;
+    auto resid_norm = [&](bool add) -> qres_status {
+        const long long* racc = add ? pending_acc.acc : nullptr;
+        pending_acc = Pending();
+        qres_status s = K(resid_norm_launch(R, cur, racc, add ? other : nullptr, c->hbuf, st, true), "resid-norm");
+        if (add) std::swap(cur, other);
+        return s;
+    };
     auto norm_gemv = [&](const qres_weight& w, int epi, void* out, int ld_out, const char* what) -> qres_status {
+        if (split && pending_acc.acc) {
+            qres_status s = resid_norm(true);
+            if (s) return s;
+            return K(gemv_launch(w, R, PRO_BF16, c->hbuf, kHidden, epi, out, ld_out, grid_of(w), c->err, st, true, nullptr,
+                                 nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&w)),
+                     what);
+        }
         if (pending_acc.acc) {
             GemvExchange ex;
             take_pending(ex);
@@ -827,16 +850,26 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             const qres_weight& wi = L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN];
             GemvExchange ei;
             const bool add = pending_acc.acc != nullptr;
-            if (add) take_pending(ei);
+            if (split) {
+                s = resid_norm(add);
+                if (s) return s;
+                ei.acc_out = accD;
+                STEP(gemv_launch(wi, R, PRO_BF16, c->hbuf, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
+                                 nullptr, nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
+                     "in-proj");
+            }
+            if (add && !split) take_pending(ei);
             ei.acc_out = accD;
             if (tp) {
                 ei.zero = accB;
                 ei.zero_words = (size_t)R * 2 * c->ic;
             }
-            STEP(gemv_launch(wi, R, add ? (tp ? 4 : 2) : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
-                             nullptr, add ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
-                 "in-proj");
-            if (add) std::swap(cur, other);
+            if (!split) {
+                STEP(gemv_launch(wi, R, add ? (tp ? 4 : 2) : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st,
+                                 true, nullptr, add ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
+                     "in-proj");
+                if (add) std::swap(cur, other);
+            }
         } else {
             s = norm_gemv(L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN], 0, c->y, c->ld_y, "in-proj");
             if (s) return s;
@@ -875,14 +908,22 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                  "out-proj");
             GemvExchange eg;
             pending_acc = producer_of(wo, XA);
-            take_pending(eg);
             eg.acc_out = accB;
             eg.zero = tp ? accD : XC;
             eg.zero_words = tp ? (size_t)R * c->ld_y : (size_t)R * kHidden;
-            STEP(gemv_launch(wg, R, tp ? 4 : 2, cur, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true, nullptr, other,
-                             c->gemv_work, c->gemv_work_bytes, next_of(&wg), &eg),
-                 "gate-up");
-            std::swap(cur, other);
+            if (split) {
+                s = resid_norm(true);
+                if (s) return s;
+                STEP(gemv_launch(wg, R, PRO_BF16, c->hbuf, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true,
+                                 nullptr, nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wg), &eg),
+                     "gate-up");
+            } else {
+                take_pending(eg);
+                STEP(gemv_launch(wg, R, tp ? 4 : 2, cur, kHidden, 5, nullptr, 2 * c->ic, grid_of(wg), c->err, st, true, nullptr,
+                                 other, c->gemv_work, c->gemv_work_bytes, next_of(&wg), &eg),
+                     "gate-up");
+                std::swap(cur, other);
+            }
             GemvExchange ed;
             ed.gacc = accB;
             ed.ld_gacc = 2 * c->ic;
