@@ -136,7 +136,7 @@ def test_gemv_swiglu_parity(cuda, rows):
 
 
 @pytest.mark.parametrize("n,r", [(1, 0), (4, 1), (8, 7)])
-@pytest.mark.parametrize("rows", [1, 2, 8])
+@pytest.mark.parametrize("rows", [1, 2, 3, 5, 8])
 def test_gdn_mixer_parity(cuda, n, r, rows):
     s = step.Shard(r, n)
     d = weights.RankDims(r, n)

@@ -49,6 +49,7 @@ struct GdnParams {
     const float* neg_a;      // [nv]
     const float* norm_w;     // [128]
     float* state;            // [B][nv][128][128]; verify: [R slots][nv][128][128] of the one user
+    int rows;                // users (the batch kernel's groups)
     int verify;              // 0, or R: the rows are R consecutive positions of one user
     const int32_t* slot0;    // verify: the state slot row 0 starts from (device, the token state)
     uint16_t* hist;          // [B][8][conv]
@@ -293,6 +294,271 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
     if (bad && tid == 0 && qtr == 0) atomicOr(p.err, kErrBounds);
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// The batch form (2 or more users, not verify): one 4-CTA cluster per (value head, group of UG users), CTA q
+// owning the same 32 columns of every user's state in the group. At 8 users the one-user form needs 1,536 CTAs
+// of which ~740 fit at once, so the launch ran in two waves of a latency-bound chain; here 384 CTAs of UG = 4
+// users fit in one (three per SM: 64 KB of state in shared memory each). Each thread copies its own 8 x 4
+// elements of every user's slice with 16-byte cp.async right after the dependency wait -- the group's 64 KB in
+// flight at once -- and reads them back itself, so no barrier guards the copies. The passes run over all users
+// of the group between the CTA's barriers (one set of barriers and two cluster barriers for the group instead of
+// per user). Same arithmetic as the one-user form; the row sums of kS and o reduce a warp's 4 row groups by
+// shuffles first, then the 4 warps in order.
+template <int UG>
+__global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads, 3)
+    gdn_batch_kernel(const GdnParams p) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int hh = blockIdx.x;       // local value head
+    const int b0 = blockIdx.y * UG;  // first user of the group
+    const int qtr = blockIdx.z;      // column quarter (= rank in the cluster)
+    const int nu = min(UG, p.rows - b0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = p.nk * kDK, gv = p.nv * kDV;
+    const int conv = 2 * gq + gv;
+    const int group = p.nv / p.nk;
+    const int kh = hh / group;
+    const int c0 = qtr * kGdnCols;
+
+    extern __shared__ __align__(16) float st[];  // [UG][128 rows][32 columns]: the users' state slices
+    __shared__ float qk[UG][2][kDK];             // conv outputs q, k (then normalised in place)
+    __shared__ float red[UG][4][kGdnCols];       // per warp row sums
+    __shared__ float dl[UG][kGdnCols];
+    __shared__ float sc[UG][4];
+    __shared__ float osq[UG];  // this CTA's sum of o^2 per user, read by the whole cluster
+
+    pdl_launch();
+    const int cq = tid & 7, rp = tid >> 3;
+    const size_t slot_stride = (size_t)p.nv * kDK * kDV;
+    auto slice = [&](int u) { return p.state + (size_t)(b0 + u) * slot_stride + (size_t)hh * kDK * kDV + c0; };
+    // immutable or L2-only work ahead of the dependency wait: the slices, taps and history into L2
+#pragma unroll
+    for (int u = 0; u < UG; ++u)
+        if (u < nu) bulk_prefetch_l2(slice(u) + (size_t)tid * kDV, kGdnCols * 4);
+    if (tid < 3 * UG) {
+        const int u = tid / 3, part = tid % 3;
+        if (u < nu) {
+            const uint16_t* h = p.hist + (size_t)(b0 + u) * QRES_HIST_SLOTS * conv;
+            const size_t ch = part == 0 ? (size_t)kh * kDK : part == 1 ? (size_t)gq + kh * kDK : (size_t)2 * gq + hh * kDV + c0;
+            const uint32_t bytes = part == 2 ? kGdnCols * 2 : kDK * 2;
+            for (int slot = 0; slot < QRES_HIST_SLOTS; ++slot) bulk_prefetch_l2(h + (size_t)slot * conv + ch, bytes);
+        }
+    }
+    if (tid == 32) {
+        bulk_prefetch_l2(p.taps + (size_t)kh * kDK * 4, kDK * 8);
+        bulk_prefetch_l2(p.taps + ((size_t)gq + kh * kDK) * 4, kDK * 8);
+        bulk_prefetch_l2(p.taps + ((size_t)2 * gq + hh * kDV + c0) * 4, kGdnCols * 8);
+    }
+    if (p.pf && tid == 64) {
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
+    }
+    pdl_wait();
+
+    int pos[UG];
+    bool bad[UG];
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        pos[u] = u < nu ? p.pos[b0 + u] : -1;
+        bad[u] = u >= nu || pos[u] < 0;
+    }
+    // ---- the state slices: this thread's rows rp*8 .. rp*8+7, columns 4cq .. 4cq+3 of each user
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        if (bad[u]) continue;
+        const float* S = slice(u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = rp * 8 + i;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(st + (u * kDK + row) * kGdnCols + 4 * cq)),
+                         "l"(S + (size_t)row * kDV + 4 * cq)
+                         : "memory");
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+
+    // ---- every other input of the group, issued together: a, b per user; z, conv inputs and history
+    const YIn yall{p.y, p.yacc};
+    const float dt_h = p.dt[hh], na_h = p.neg_a[hh];
+    const float nw_c = p.norm_w[c0 + lane];
+    const int vu = warp;  // this thread's v channel: column `lane` of user `warp`; the pass-4/5 user of the warp
+    const int chq = kh * kDK + tid, chk = gq + kh * kDK + tid, chv = 2 * gq + hh * kDV + c0 + lane;
+    const int a_off = 2 * gq + 2 * gv;
+    uint16_t a_raw[UG], yq[UG], yk[UG], hq[UG][3], hk[UG][3];
+    uint16_t b_raw = 0, z_raw = 0, yv = 0, hv[3] = {0, 0, 0};
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        a_raw[u] = yq[u] = yk[u] = 0;
+        if (bad[u]) continue;
+        const YIn y = yall.at((size_t)(b0 + u) * p.ld_y);
+        const uint16_t* hist = p.hist + (size_t)(b0 + u) * QRES_HIST_SLOTS * conv;
+        a_raw[u] = y[a_off + hh];
+        yq[u] = y[chq];
+        yk[u] = y[chk];
+#pragma unroll
+        for (int jj = 0; jj < 3; ++jj) {
+            const size_t sl = (size_t)((pos[u] - 3 + jj + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv;
+            hq[u][jj] = hist[sl + chq];
+            hk[u][jj] = hist[sl + chk];
+        }
+    }
+    const int posv = vu < nu ? p.pos[b0 + vu] : -1;  // the v user's position (no dynamic index into pos[])
+    const bool vok = posv >= 0;
+    if (vok) {
+        const YIn y = yall.at((size_t)(b0 + vu) * p.ld_y);
+        const uint16_t* hist = p.hist + (size_t)(b0 + vu) * QRES_HIST_SLOTS * conv;
+        b_raw = y[a_off + p.nv + hh];
+        z_raw = y[2 * gq + gv + hh * kDV + c0 + lane];
+        yv = y[chv];
+#pragma unroll
+        for (int jj = 0; jj < 3; ++jj) hv[jj] = hist[(size_t)((posv - 3 + jj + QRES_HIST_SLOTS) % QRES_HIST_SLOTS) * conv + chv];
+    }
+    const uint2 tq = *reinterpret_cast<const uint2*>(p.taps + (size_t)chq * 4);
+    const uint2 tk = *reinterpret_cast<const uint2*>(p.taps + (size_t)chk * 4);
+    const uint2 tv = *reinterpret_cast<const uint2*>(p.taps + (size_t)chv * 4);
+
+    // ---- conv1d + SiLU (bf16 window, round-to-nearest taps as the one-user form)
+    auto conv4 = [](uint16_t h0, uint16_t h1, uint16_t h2, uint16_t x, uint2 t) {
+        float acc = mul_rn(__uint_as_float((uint32_t)h0 << 16), bf16lo(t.x));
+        acc = add_rn(acc, mul_rn(__uint_as_float((uint32_t)h1 << 16), bf16hi(t.x)));
+        acc = add_rn(acc, mul_rn(__uint_as_float((uint32_t)h2 << 16), bf16lo(t.y)));
+        acc = add_rn(acc, mul_rn(__uint_as_float((uint32_t)x << 16), bf16hi(t.y)));
+        return bf16_round(silu_f(acc));
+    };
+    const bool qk_writer = hh % group == 0 && qtr == 0;  // one writer per q / k history element
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        if (bad[u]) continue;
+        qk[u][0][tid] = conv4(hq[u][0], hq[u][1], hq[u][2], yq[u], tq);
+        qk[u][1][tid] = conv4(hk[u][0], hk[u][1], hk[u][2], yk[u], tk);
+        if (qk_writer) {
+            uint16_t* hist = p.hist + ((size_t)(b0 + u) * QRES_HIST_SLOTS + pos[u] % QRES_HIST_SLOTS) * conv;
+            hist[chq] = yq[u];
+            hist[chk] = yk[u];
+        }
+    }
+    const float vconv = vok ? conv4(hv[0], hv[1], hv[2], yv, tv) : 0.f;
+    if (vok) p.hist[((size_t)(b0 + vu) * QRES_HIST_SLOTS + posv % QRES_HIST_SLOTS) * conv + chv] = yv;
+    float decay[UG];
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        const float av = __uint_as_float((uint32_t)a_raw[u] << 16);
+        decay[u] = bad[u] ? 0.f : expf(mul_rn(na_h, softplus_f(add_rn(av, dt_h))));
+    }
+    __syncthreads();
+    // ---- l2 norms of q and k (the one-user form's pairing: warp w sums half w & 1 of q (w < 2) or k)
+    {
+        const int which = warp >> 1, h0 = (warp & 1) * 64;
+#pragma unroll
+        for (int u = 0; u < UG; ++u) {
+            if (bad[u]) continue;
+            const float v0 = qk[u][which][h0 + lane], v1 = qk[u][which][h0 + 32 + lane];
+            const float ss = warp_sum(v0 * v0 + v1 * v1);
+            if (lane == 0) sc[u][warp] = ss;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        if (bad[u]) continue;
+        const float rq = rsqrt_ieee(sc[u][0] + sc[u][1] + 1e-6f), rk = rsqrt_ieee(sc[u][2] + sc[u][3] + 1e-6f);
+        qk[u][0][tid] = mul_rn(mul_rn(qk[u][0][tid], rq), 0.08838834764831845f);
+        qk[u][1][tid] = mul_rn(qk[u][1][tid], rk);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's own copies: it alone reads them
+    __syncthreads();
+    auto row_sums = [&](int u, float* part) {
+        // the 4 row groups of the warp (lanes cq, cq + 8, cq + 16, cq + 24), then one word per warp
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 8);
+            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 16);
+        }
+        if (lane < 8) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[u][warp][4 * cq + j] = part[j];
+        }
+    };
+    // ---- pass 1: kS = (decay * kn) @ S
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        if (bad[u]) continue;
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 s = *reinterpret_cast<const float4*>(st + (u * kDK + rp * 8 + i) * kGdnCols + 4 * cq);
+            const float dk = mul_rn(decay[u], qk[u][1][rp * 8 + i]);
+            part[0] = fmaf(dk, s.x, part[0]);
+            part[1] = fmaf(dk, s.y, part[1]);
+            part[2] = fmaf(dk, s.z, part[2]);
+            part[3] = fmaf(dk, s.w, part[3]);
+        }
+        row_sums(u, part);
+    }
+    __syncthreads();
+    // ---- pass 2: delta = beta * (v - kS), thread (user warp, column lane)
+    if (vok) {
+        const float beta = sigmoid_f(__uint_as_float((uint32_t)b_raw << 16));
+        const float t = ((red[vu][0][lane] + red[vu][1][lane]) + red[vu][2][lane]) + red[vu][3][lane];
+        dl[vu][lane] = mul_rn(beta, vconv - t);
+    }
+    __syncthreads();
+    // ---- pass 3: S <- decay * S + kn (x) delta (written back to HBM), o = qn @ S
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+        if (bad[u]) continue;
+        float* S = slice(u);
+        const float d0 = dl[u][4 * cq], d1 = dl[u][4 * cq + 1], d2 = dl[u][4 * cq + 2], d3 = dl[u][4 * cq + 3];
+        const float dec = decay[u];
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = rp * 8 + i;
+            const float kn = qk[u][1][row], qn = qk[u][0][row];
+            float4 v = *reinterpret_cast<const float4*>(st + (u * kDK + row) * kGdnCols + 4 * cq);
+            v.x = add_rn(mul_rn(dec, v.x), mul_rn(kn, d0));
+            v.y = add_rn(mul_rn(dec, v.y), mul_rn(kn, d1));
+            v.z = add_rn(mul_rn(dec, v.z), mul_rn(kn, d2));
+            v.w = add_rn(mul_rn(dec, v.w), mul_rn(kn, d3));
+            reinterpret_cast<float4*>(S + (size_t)row * kDV)[cq] = v;
+            part[0] = fmaf(qn, v.x, part[0]);
+            part[1] = fmaf(qn, v.y, part[1]);
+            part[2] = fmaf(qn, v.z, part[2]);
+            part[3] = fmaf(qn, v.w, part[3]);
+        }
+        __syncwarp();  // red[u][warp] of pass 1 was read in pass 2 behind the barrier; rewritten now
+        row_sums(u, part);
+    }
+    __syncthreads();
+    // ---- pass 4: o of (user warp, column lane) and the CTA's sum of o^2 per user
+    float ov = 0.f;
+    if (vok) {
+        ov = ((red[vu][0][lane] + red[vu][1][lane]) + red[vu][2][lane]) + red[vu][3][lane];
+        const float sq = warp_sum(ov * ov);
+        if (lane == 0) osq[vu] = sq;
+    }
+    // ---- gated RMSNorm: the head's 4 CTAs' sums through distributed shared memory
+    cluster.sync();
+    if (vok) {
+        float tot = 0.f;
+#pragma unroll
+        for (int r = 0; r < kGdnSplit; ++r) tot += *cluster.map_shared_rank(&osq[vu], r);
+        const float rr = rsqrt_ieee(tot / (float)kDV + kEps);
+        const float on = mul_rn(mul_rn(ov, rr), nw_c);
+        const float z = __uint_as_float((uint32_t)z_raw << 16);
+        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(on, silu_f(z)));
+        const size_t idx = (size_t)(b0 + vu) * gv + hh * kDV + c0 + lane;
+        reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
+        if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
+    }
+    cluster.sync();  // no CTA leaves while a peer may still read its osq
+    if (tid == 0 && qtr == 0) {
+        bool any = false;
+#pragma unroll
+        for (int u = 0; u < UG; ++u) any = any || (u < nu && pos[u] < 0);
+        if (any) atomicOr(p.err, kErrBounds);
+    }
+}
+
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -317,6 +583,7 @@ cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const 
     p.pf = static_cast<const uint8_t*>(pf);
     p.pf_bytes = pf_bytes;
     p.err = err;
+    p.rows = rows;
     p.verify = verify;
     p.slot0 = slot0;
     cudaLaunchConfig_t cfg = {};
@@ -328,6 +595,20 @@ cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const 
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
+    if (!verify && rows > 1) {
+        // the batch form: groups of 2 users up to 4 rows, of 4 above
+        const int ug = rows <= 4 ? 2 : 4;
+        cfg.gridDim = dim3(p.nv, (rows + ug - 1) / ug, kGdnSplit);
+        cfg.dynamicSmemBytes = (size_t)ug * kDK * kGdnCols * sizeof(float);
+        auto k = ug == 2 ? gdn_batch_kernel<2> : gdn_batch_kernel<4>;
+        static bool smem_set[2] = {false, false};
+        if (!smem_set[ug / 4]) {
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+            if (e != cudaSuccess) return e;
+            smem_set[ug / 4] = true;
+        }
+        return cudaLaunchKernelEx(&cfg, k, p);
+    }
     return cudaLaunchKernelEx(&cfg, gdn_decode_kernel, p);
 }
 
