@@ -480,12 +480,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     __syncthreads();
     if (!last_flag) return;
-    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate. The chunk
-    // weights are computed once in shared memory; every thread then sums its dimension over the chunks with
-    // independent loads.
+    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate. Every load
+    // of the combine is independent, so they go out in wide rounds (each an L2 round trip): the chunks' (m, l)
+    // into shared memory in one, then each thread's dimension of every head over 8 chunks at a time.
     const float* base = p.part + (((size_t)b * p.nkv + g) * p.nchunks) * G * (2 + kHD);
-    float* wch = reinterpret_cast<float*>(ring + kStageBytes);  // [nchunks][G] chunk weights
-    for (int i = tid; i < nce * G; i += kAttnThreads) wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
+    float* wch = reinterpret_cast<float*>(ring + kStageBytes);  // [nchunks][G] chunk maxima, then weights
+    float* lch = wch + p.nchunks * G;                            // [nchunks][G] chunk sums
+    for (int i = tid; i < nce * G; i += kAttnThreads) {
+        wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
+        lch[i] = __ldcg(base + (size_t)i * (2 + kHD) + 1);
+    }
     __syncthreads();
     if (tid < G) {
         float M = -INFINITY;
@@ -495,28 +499,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const float mc = wch[cc * G + tid];
             const float w = mc == -INFINITY ? 0.f : expf(mc - M);
             wch[cc * G + tid] = w;
-            Lsum = fmaf(w, __ldcg(base + ((size_t)cc * G + tid) * (2 + kHD) + 1), Lsum);
+            Lsum = fmaf(w, lch[cc * G + tid], Lsum);
         }
         lrow[tid] = Lsum;
     }
     __syncthreads();
-    for (int j = 0; j < G; ++j) {
-        float Ov = 0.f;
-        // chunk weights applied in chunk order; the loads of 4 chunks in flight at once
-        for (int cc = 0; cc < nce; cc += 4) {
-            float ov[4];
+    constexpr int kCU = 8;  // chunks per round
+    float Ov[kMaxGroup];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                ov[u] = cc + u < nce ? __ldcg(base + ((size_t)(cc + u) * G + j) * (2 + kHD) + 2 + tid) : 0.f;
+    for (int j = 0; j < kMaxGroup; ++j) Ov[j] = 0.f;
+    for (int cc = 0; cc < nce; cc += kCU) {
+        float ov[kCU][kMaxGroup];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float w = cc + u < nce ? wch[(cc + u) * G + j] : 0.f;
-                if (w != 0.f) Ov = fmaf(w, ov[u], Ov);
+        for (int u = 0; u < kCU; ++u)
+#pragma unroll
+            for (int j = 0; j < kMaxGroup; ++j)
+                ov[u][j] = (j < G && cc + u < nce) ? __ldcg(base + ((size_t)(cc + u) * G + j) * (2 + kHD) + 2 + tid) : 0.f;
+        // chunk weights applied in chunk order
+#pragma unroll
+        for (int u = 0; u < kCU; ++u)
+#pragma unroll
+            for (int j = 0; j < kMaxGroup; ++j) {
+                const float w = (j < G && cc + u < nce) ? wch[(cc + u) * G + j] : 0.f;
+                if (w != 0.f) Ov[j] = fmaf(w, ov[u][j], Ov[j]);
             }
-        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) {
+        if (j >= G) break;
         const int hq = g * G + j;
         const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);
-        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(Ov / lrow[j], sigmoid_f(gate)));
+        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(Ov[j] / lrow[j], sigmoid_f(gate)));
         const size_t idx = (size_t)b * p.h * kHD + hq * kHD + tid;
         reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
         if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;

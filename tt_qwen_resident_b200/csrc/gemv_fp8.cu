@@ -773,12 +773,38 @@ static cudaError_t launch_pe(const GemvParams& p, int Bt, int grid, size_t smem,
 // 640 threads x 8 consecutive elements.
 constexpr int kResidThreads = kHidden / 8;
 
+// Over ranks (rc_ranks > 0) racc holds counted words -- (value << 8) + contributions, added by every rank's
+// row-parallel epilogue -- and the CTA first sweeps its user's words (bounded) until each holds rc_ranks x (the
+// producing launch's CTAs over the word's tile) contributions (the producer split its units as rc_base / rc_rem,
+// rc_nkb K blocks per tile).
 __global__ void __launch_bounds__(kResidThreads) resid_norm_kernel(const float* x, const long long* racc, float* x_out,
-                                                                    uint16_t* h) {
+                                                                    uint16_t* h, int rc_ranks, int rc_base, int rc_rem,
+                                                                    int rc_nkb, uint32_t* err) {
     const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ float red[kResidThreads / 32];
     pdl_launch();
     pdl_wait();
+    if (racc != nullptr && rc_ranks > 0) {
+        // this thread's 8 words lie in one 128-row tile
+        const int T = (8 * tid) / kTileRows;
+        const uint32_t want = (uint32_t)rc_ranks * (uint32_t)(cta_of_unit(T * rc_nkb + rc_nkb - 1, rc_base, rc_rem) -
+                                                              cta_of_unit(T * rc_nkb, rc_base, rc_rem) + 1);
+        const long long* a = racc + (size_t)b * kHidden + 8 * tid;
+        for (uint32_t it = 0;; ++it) {
+            bool mine = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 v = ld_volatile128(a + 2 * j);
+                mine = mine && (v.x & 255u) == want && (v.z & 255u) == want;
+            }
+            if (__syncthreads_and(mine)) break;
+            if (it >= kPeerSpinLimit / 64) {
+                if (tid == 0) atomicOr(err, kErrPeer | kErrTimeout);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
     const float4* xs = reinterpret_cast<const float4*>(x + (size_t)b * kHidden) + 2 * tid;
     float v[8];
     const float4 a0 = xs[0], a1 = xs[1];
@@ -791,8 +817,8 @@ __global__ void __launch_bounds__(kResidThreads) resid_norm_kernel(const float* 
         for (int j = 0; j < 4; ++j) q[j] = __ldcg(ra + j);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            v[2 * j] += acc_decode(q[j].x);
-            v[2 * j + 1] += acc_decode(q[j].y);
+            v[2 * j] += rc_ranks > 0 ? acc_decode_cnt(q[j].x) : acc_decode(q[j].x);
+            v[2 * j + 1] += rc_ranks > 0 ? acc_decode_cnt(q[j].y) : acc_decode(q[j].y);
         }
         float4* xo = reinterpret_cast<float4*>(x_out + (size_t)b * kHidden) + 2 * tid;
         xo[0] = make_float4(v[0], v[1], v[2], v[3]);
@@ -817,8 +843,18 @@ __global__ void __launch_bounds__(kResidThreads) resid_norm_kernel(const float* 
 }
 
 cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, float* x_out, uint16_t* h,
-                              cudaStream_t st, bool pdl) {
+                              cudaStream_t st, bool pdl, const GemvExchange* ex, uint32_t* err) {
     if (users < 1 || users > kMaxRows || (racc && !x_out)) return cudaErrorInvalidValue;
+    int rc_ranks = 0, rc_base = 0, rc_rem = 0, rc_nkb = 0;
+    if (ex != nullptr && ex->rc_ranks > 0) {
+        // the counted words of a producer whose partition is given (as gemv_launch checks it)
+        if (racc == nullptr || err == nullptr || ex->rc_grid < 1 || ex->rc_nkb < 1 || ex->rc_units < ex->rc_grid)
+            return cudaErrorInvalidValue;
+        rc_ranks = ex->rc_ranks;
+        rc_base = ex->rc_units / ex->rc_grid;
+        rc_rem = ex->rc_units % ex->rc_grid;
+        rc_nkb = ex->rc_nkb;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(users);
     cfg.blockDim = dim3(kResidThreads);
@@ -828,7 +864,7 @@ cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, 
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, resid_norm_kernel, x, racc, x_out, h);
+    return cudaLaunchKernelEx(&cfg, resid_norm_kernel, x, racc, x_out, h, rc_ranks, rc_base, rc_rem, rc_nkb, err);
 }
 
 // shared memory of one GEMV CTA: half an SM's (a second CTA -- the next projection's, under programmatic

@@ -30,7 +30,7 @@ size_t gemv_workspace_bytes(int grid);
 int gemv_grid(int users, int rows_pad, int K, int grid);
 int gemv_group_blocks(int users, int epi, int K);
 cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, float* x_out, uint16_t* h,
-                              cudaStream_t st, bool pdl);
+                              cudaStream_t st, bool pdl, const GemvExchange* ex, uint32_t* err);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
                        const float* dt, const float* neg_a, const float* norm_w, float* state, uint16_t* hist,
                        uint16_t* o, uint16_t* mixer_copy, uint32_t* err, cudaStream_t st, bool pdl,
@@ -749,14 +749,17 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
         ex.rc_nkb = pending_acc.nkb;
         pending_acc = Pending();
     };
-    // One rank at 4 or more rows: a projection's rmsnorm input is formed once per user (resid_norm: x + the pending
-    // sums -> the other residual buffer, h = bf16(rmsnorm) -> hbuf) and the projection reads its window of h,
-    // instead of each of its CTAs re-reading every user's residual and sums (~480 KB per CTA at 8 rows).
-    const bool split = accm && !tp && R >= 4;
+    // 4 or more rows: a projection's rmsnorm input is formed once per user (resid_norm: x + the pending sums -- over
+    // ranks the counted words, once complete -> the other residual buffer, h = bf16(rmsnorm) -> hbuf) and the
+    // projection reads its window of h, instead of each of its CTAs re-reading every user's residual and sums
+    // (~480 KB per CTA at 8 rows).
+    const bool split = accm && R >= 4;
     auto resid_norm = [&](bool add) -> qres_status {
-        const long long* racc = add ? pending_acc.acc : nullptr;
+        GemvExchange ex;
+        if (add) take_pending(ex);
         pending_acc = Pending();
-        qres_status s = K(resid_norm_launch(R, cur, racc, add ? other : nullptr, c->hbuf, st, true), "resid-norm");
+        qres_status s = K(resid_norm_launch(R, cur, ex.racc, add ? other : nullptr, c->hbuf, st, true, &ex, c->err),
+                          "resid-norm");
         if (add) std::swap(cur, other);
         return s;
     };
@@ -850,21 +853,19 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             const qres_weight& wi = L.w[at ? QRES_W_ATTN_IN : QRES_W_GDN_IN];
             GemvExchange ei;
             const bool add = pending_acc.acc != nullptr;
-            if (split) {
-                s = resid_norm(add);
-                if (s) return s;
-                ei.acc_out = accD;
-                STEP(gemv_launch(wi, R, PRO_BF16, c->hbuf, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
-                                 nullptr, nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
-                     "in-proj");
-            }
-            if (add && !split) take_pending(ei);
             ei.acc_out = accD;
             if (tp) {
                 ei.zero = accB;
                 ei.zero_words = (size_t)R * 2 * c->ic;
             }
-            if (!split) {
+            if (split) {
+                s = resid_norm(add);
+                if (s) return s;
+                STEP(gemv_launch(wi, R, PRO_BF16, c->hbuf, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st, true,
+                                 nullptr, nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
+                     "in-proj");
+            } else {
+                if (add) take_pending(ei);
                 STEP(gemv_launch(wi, R, add ? (tp ? 4 : 2) : 0, cur, kHidden, 5, nullptr, c->ld_y, grid_of(wi), c->err, st,
                                  true, nullptr, add ? other : nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wi), &ei),
                      "in-proj");
