@@ -233,7 +233,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     const int L = pos + 1;
     const int npg = (L + kKvBlock - 1) / kKvBlock;
-    const int ppc = (npg + p.nchunks - 1) / p.nchunks;
+    // at least one page per page group: the groups of a CTA take their pages in parallel, so a chunk of 3 pages
+    // costs what a chunk of 1 does, and a short context leaves fewer chunks to combine
+    const int ppc = max((npg + p.nchunks - 1) / p.nchunks, min(kAttnGroups, npg));
     const int pg0 = c * ppc, pg1 = min(pg0 + ppc, npg);
     // chunks that hold pages at this length: the others leave at once (no partial, no ticket), so a short
     // context costs what its pages do
@@ -448,7 +450,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
     }
     __syncthreads();
-    // partial of this chunk: per head (max, sum, o[256])
+    // partial of this chunk: per head (max, sum, o[256]); a single chunk is the result itself (the combine's
+    // weights would be exp(0) = 1: the same arithmetic)
     float* part = p.part + ((((size_t)b * p.nkv + g) * p.nchunks + c) * G) * (2 + kHD);
     for (int j = 0; j < G; ++j) {
         float M = -INFINITY;
@@ -462,12 +465,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             Ls = fmaf(wq_, lg[q * 8 + j], Ls);
             ov = fmaf(wq_, Og[(q * 8 + j) * kHD + tid], ov);
         }
+        if (nce == 1) {
+            const int hq = g * G + j;
+            const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);
+            const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(ov / Ls, sigmoid_f(gate)));
+            const size_t idx = (size_t)b * p.h * kHD + hq * kHD + tid;
+            reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
+            if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
+            continue;
+        }
         if (tid == 0) {
             part[j * (2 + kHD)] = M;
             part[j * (2 + kHD) + 1] = Ls;
         }
         part[j * (2 + kHD) + 2 + tid] = ov;
     }
+    if (nce == 1) return;
     // release / acquire through one thread: the barrier orders every thread's stores before thread 0's fence
     // (cumulative) and atomic; the last CTA's fence before the barrier orders the other CTAs' parts before its
     // threads' reads (a fence in every thread costs microseconds)

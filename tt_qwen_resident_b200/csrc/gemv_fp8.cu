@@ -351,7 +351,42 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
         for (int b = 0; b < B; ++b) {
             float ss = 0.f;
             if (b < users) {
-                if (regs) {
+                // the hidden-size row plus fixed-point sums (the step's rmsnorm prologue): every load of the row issued
+                // before any is used -- a load behind a per-iteration branch would cost one L2 round trip per
+                // iteration (the operand build waits on this)
+                constexpr int kXh = kHidden / (4 * kGemvThreads);  // 5
+                if (regs && K == kHidden && kAdd && p.tagged == nullptr && p.racc != nullptr) {
+                    longlong2 q[kXh][2];
+#pragma unroll
+                    for (int j = 0; j < kXh; ++j) {
+                        const int i = tid + j * kGemvThreads;
+                        xr[kRegs ? b : 0][j] = reinterpret_cast<const float4*>(p.x + (size_t)b * K)[i];
+                        const longlong2* a = reinterpret_cast<const longlong2*>(p.racc + (size_t)b * K + 4 * i);
+                        q[j][0] = __ldcg(a);
+                        q[j][1] = __ldcg(a + 1);
+                    }
+#pragma unroll
+                    for (int j = 0; j < kXh; ++j) {
+                        const int i = tid + j * kGemvThreads;
+                        float4 v = xr[kRegs ? b : 0][j];
+                        if (PRO == PRO_RMSNORM_XACC) {
+                            v.x += acc_decode_cnt(q[j][0].x);
+                            v.y += acc_decode_cnt(q[j][0].y);
+                            v.z += acc_decode_cnt(q[j][1].x);
+                            v.w += acc_decode_cnt(q[j][1].y);
+                        } else {
+                            v.x += acc_decode(q[j][0].x);
+                            v.y += acc_decode(q[j][0].y);
+                            v.z += acc_decode(q[j][1].x);
+                            v.w += acc_decode(q[j][1].y);
+                        }
+                        if (blockIdx.x == 0) reinterpret_cast<float4*>(p.x_out + (size_t)b * K)[i] = v;
+                        xr[kRegs ? b : 0][j] = v;
+                        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    }
+#pragma unroll
+                    for (int j = kXh; j < kXj; ++j) xr[kRegs ? b : 0][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else if (regs) {
 #pragma unroll
                     for (int j = 0; j < kXj; ++j) {
                         const int i = tid + j * kGemvThreads;
