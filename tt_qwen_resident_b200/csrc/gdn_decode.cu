@@ -86,11 +86,11 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
     const int nrows = R ? R : 1;
     const size_t slot_stride = (size_t)p.nv * kDK * kDV;
     // Before griddepcontrol.wait only immutable data may be read (an earlier kernel of the stream may still be
-    // running); an L2 prefetch of the slice is safe (L2 is the point of coherence) and starts its 16 KB early.
-    if (!R && tid < kDK) {
-        const float* S0 = p.state + (((size_t)b * p.nv + hh) * kDK) * kDV + c0;
-        bulk_prefetch_l2(S0 + (size_t)tid * kDV, kGdnCols * 4);
-    }
+    // running); an L2 prefetch of the state is safe (L2 is the point of coherence) and starts its 16 KB early.
+    // The cluster's CTAs prefetch the head's 64 KB as four contiguous quarters (rows 32 q .. 32 q + 31), one bulk
+    // prefetch each: a prefetch per 128-byte row of the CTA's own columns would queue 128 small operations.
+    if (!R && tid == 0)
+        bulk_prefetch_l2(p.state + ((((size_t)b * p.nv + hh) * kDK) + 32 * qtr) * kDV, 32 * kDV * 4);
     // the conv taps (immutable) and every slot of this CTA's conv-history channels (written only by this kernel,
     // a step earlier) into L2 as well: q and k of the key head (2 x 256 B per slot), v of the CTA's 32 columns
     if (tid >= kDK - 3 * 8 && tid < kDK) {
@@ -330,10 +330,10 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
     const int cq = tid & 7, rp = tid >> 3;
     const size_t slot_stride = (size_t)p.nv * kDK * kDV;
     auto slice = [&](int u) { return p.state + (size_t)(b0 + u) * slot_stride + (size_t)hh * kDK * kDV + c0; };
-    // immutable or L2-only work ahead of the dependency wait: the slices, taps and history into L2
-#pragma unroll
-    for (int u = 0; u < UG; ++u)
-        if (u < nu) bulk_prefetch_l2(slice(u) + (size_t)tid * kDV, kGdnCols * 4);
+    // immutable or L2-only work ahead of the dependency wait: the state, taps and history into L2 (the state as
+    // the head's contiguous quarter q, one bulk prefetch per user: the cluster covers the head)
+    if (tid < nu)
+        bulk_prefetch_l2(p.state + (size_t)(b0 + tid) * slot_stride + ((size_t)hh * kDK + 32 * qtr) * kDV, 32 * kDV * 4);
     if (tid < 3 * UG) {
         const int u = tid / 3, part = tid % 3;
         if (u < nu) {
@@ -347,10 +347,6 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
         bulk_prefetch_l2(p.taps + (size_t)kh * kDK * 4, kDK * 8);
         bulk_prefetch_l2(p.taps + ((size_t)gq + kh * kDK) * 4, kDK * 8);
         bulk_prefetch_l2(p.taps + ((size_t)2 * gq + hh * kDV + c0) * 4, kGdnCols * 8);
-    }
-    if (p.pf && tid == 64) {
-        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
-        l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
     }
     pdl_wait();
 
@@ -466,6 +462,12 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's own copies: it alone reads them
     __syncthreads();
+    // the following projection's weights into L2 while the passes run: issued once this kernel's own loads have
+    // landed, so the prefetch does not queue ahead of them
+    if (p.pf && tid == 64) {
+        const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
+    }
     auto row_sums = [&](int u, float* part) {
         // the 4 row groups of the warp (lanes cq, cq + 8, cq + 16, cq + 24), then one word per warp
 #pragma unroll
