@@ -45,6 +45,7 @@ constexpr int kMaxGroup = 6;  // query heads per KV head on a rank (24 / 4)
 constexpr int kPageBytes = kKvBlock * kHD * 2;  // 32 KB per head page of K (or V)
 constexpr int kStageBytes = 2 * kPageBytes;     // K page then V page, 4 swizzled boxes of 8 KB each
 constexpr int kBoxBytes = kKvBlock * 128;       // one TMA box: 64 rows x 64 dims bf16
+constexpr int kPartStride = 2 + kHD;  // a chunk's partial per head: max, sum, o[256]
 // dynamic shared memory: the ring, q (16 rows x 256 bf16, swizzled), the new rows' k and v (bf16), barriers
 constexpr int kOffQ = kAttnStages * kStageBytes;
 constexpr int kOffKnew = kOffQ + 16 * kHD * 2;
@@ -119,11 +120,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__device__ __forceinline__ void rms_rope_head(const YIn src, const float* w, const float* cs, const float* sn,
-                                              float* dst, float* red, bool round_bf16) {
-    // one head of 256 dims by 256 threads: dst = rope(rmsnorm(src) * w) (optionally rounded to bf16)
+__device__ __forceinline__ void rms_rope_head(float v, float wd, float c, float s, float* dst, float* red, bool round_bf16) {
+    // one head of 256 dims by 256 threads (v: this thread's dim d of the input, wd the weight there, c / s the
+    // rope cos / sin of the dim for d < 32): dst = rope(rmsnorm(src) * w) (optionally rounded to bf16)
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
-    const float v = __uint_as_float((uint32_t)src[d] << 16);
     float ss = warp_sum(v * v);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
@@ -131,12 +131,11 @@ __device__ __forceinline__ void rms_rope_head(const YIn src, const float* w, con
 #pragma unroll
     for (int i = 0; i < 8; ++i) t += red[i];
     const float r = rsqrt_ieee(t / (float)kHD + kEps);
-    const float nv = mul_rn(mul_rn(v, r), w[d]);
+    const float nv = mul_rn(mul_rn(v, r), wd);
     dst[d] = nv;
     __syncthreads();
     if (d < kRot / 2) {
         const float a = dst[d], b = dst[d + kRot / 2];
-        const float c = cs[d], s = sn[d];
         const float ra = mul_rn(a, c) - mul_rn(b, s);
         const float rb = mul_rn(b, c) + mul_rn(a, s);
         dst[d] = round_bf16 ? bf16_round(ra) : ra;
@@ -147,20 +146,12 @@ __device__ __forceinline__ void rms_rope_head(const YIn src, const float* w, con
     __syncthreads();
 }
 
-// the G query heads of a group at once (256 threads, one dim each): dst[j] = rope(rmsnorm(src_j) * w), fp32; all
-// loads in flight together and one reduction round for every head
-__device__ __forceinline__ void rms_rope_group(const YIn src, int G, const float* w, const float* cs,
-                                               const float* sn, float (*dst)[kHD], float (*red)[kMaxGroup]) {
+// the G query heads of a group at once (256 threads, one dim each): dst[j] = rope(rmsnorm(src_j) * w), fp32, one
+// reduction round for every head; v[j] = this thread's dim of head j, wd the weight there, c / s the rope cos / sin
+// of the dim (d < 32)
+__device__ __forceinline__ void rms_rope_group(const float* v, int G, float wd, float c, float s, float (*dst)[kHD],
+                                               float (*red)[kMaxGroup]) {
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
-    float v[kMaxGroup];
-#pragma unroll
-    for (int j = 0; j < kMaxGroup; ++j) v[j] = j < G ? __uint_as_float((uint32_t)src[(size_t)j * kHD + d] << 16) : 0.f;
-    const float wd = w[d];
-    float c = 0.f, s = 0.f;
-    if (d < kRot / 2) {
-        c = cs[d];
-        s = sn[d];
-    }
 #pragma unroll
     for (int j = 0; j < kMaxGroup; ++j) {
         const float ss = warp_sum(v[j] * v[j]);
@@ -223,8 +214,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
     }
+    const float wq_d = p.wq[tid], wk_d = p.wk[tid];  // immutable: read before the dependency wait
     pdl_wait();
 
+    // Every input that does not depend on the position goes out with the position's load (one L2 round trip, not
+    // a chain of them): the group's q rows, their gates, this row's new k and v. What depends on the position
+    // (page table entries, rope cos / sin) is the second round.
+    const YIn yall{p.y, p.yacc};
+    const YIn y = yall.at((size_t)b * p.ld_y);
+    const int kbase = 2 * p.h * kHD;
+    float qin[kMaxGroup], gin[kMaxGroup];
+#pragma unroll
+    for (int j = 0; j < kMaxGroup; ++j) {
+        const int hq = g * G + j;
+        qin[j] = j < G ? __uint_as_float((uint32_t)y[(size_t)hq * kHD + tid] << 16) : 0.f;
+        gin[j] = j < G ? __uint_as_float((uint32_t)y[(size_t)(p.h + hq) * kHD + tid] << 16) : 0.f;
+    }
+    const float kin = __uint_as_float((uint32_t)y[kbase + (size_t)g * kHD + tid] << 16);
+    const uint16_t vin = y[kbase + (size_t)(p.nkv + g) * kHD + tid];
     const int pos = p.pos[b];
     const int p0 = p.verify ? p.pos[0] : pos;  // first position this step writes (new k / v from p0 on)
     if (pos < 0 || pos >= p.max_pos || pos / kKvBlock >= p.max_pages || (p.verify && pos != p0 + b)) {
@@ -242,10 +249,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int nce = (npg + ppc - 1) / ppc;
     if (c >= nce) return;
     const int* pt = p.page_table + (size_t)(p.verify ? 0 : b) * p.max_pages;
-    const YIn yall{p.y, p.yacc};
-    const YIn y = yall.at((size_t)b * p.ld_y);
     const float* cs = p.cos_tab + (size_t)pos * (kRot / 2);
     const float* sn = p.sin_tab + (size_t)pos * (kRot / 2);
+    const float cpos = tid < kRot / 2 ? cs[tid] : 0.f, spos = tid < kRot / 2 ? sn[tid] : 0.f;
     const size_t head_stride = (size_t)kKvBlock * kHD;  // elements per (page, head)
 
     const int npages = max(pg1 - pg0, 0);
@@ -278,7 +284,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // q of the group's heads (fp32), then its bf16 hi / lo rows for the tensor cores
     {
         __shared__ float redg[8][kMaxGroup];
-        rms_rope_group(y.at((size_t)(g * G) * kHD), G, p.wq, cs, sn, qf, redg);
+        rms_rope_group(qin, G, wq_d, cpos, spos, qf, redg);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -289,17 +295,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(q_s) + q_off(j, ch))[e] = hi;
         reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(q_s) + q_off(j + 8, ch))[e] = lo;
     }
-    // k / v of the new positions p0 .. pos whose pages this CTA covers (row j's from its own y row)
-    const int kbase = 2 * p.h * kHD;
+    // k / v of the new positions p0 .. pos whose pages this CTA covers (row j's from its own y row; one step
+    // writes the single row pos, whose inputs are loaded already)
     const int pg_lo = pg0 * kKvBlock, pg_hi = pg1 * kKvBlock;  // positions of this CTA's pages
     const int t_lo = max(p0, pg_lo), t_hi = min(pos, pg_hi - 1);
     for (int t = t_lo; t <= t_hi; ++t) {
         const int j = t - p0;
         const YIn yj = yall.at((size_t)(p.verify ? j : b) * p.ld_y);
-        rms_rope_head(yj.at(kbase + (size_t)g * kHD), p.wk, p.cos_tab + (size_t)t * (kRot / 2),
-                      p.sin_tab + (size_t)t * (kRot / 2), kf, red, true);
+        const float kv = p.verify ? __uint_as_float((uint32_t)yj[kbase + (size_t)g * kHD + tid] << 16) : kin;
+        float ct = cpos, st = spos;  // one step: t = pos
+        if (p.verify && tid < kRot / 2) {
+            ct = p.cos_tab[(size_t)t * (kRot / 2) + tid];
+            st = p.sin_tab[(size_t)t * (kRot / 2) + tid];
+        }
+        rms_rope_head(kv, wk_d, ct, st, kf, red, true);
         knew_s[j * kHD + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(kf[tid]));
-        vnew_s[j * kHD + tid] = yj[kbase + p.nkv * kHD + g * kHD + tid];
+        vnew_s[j * kHD + tid] = p.verify ? yj[kbase + (size_t)(p.nkv + g) * kHD + tid] : vin;
         __syncthreads();  // kf is reused by the next row
     }
     if (pg0 <= pos / kKvBlock && pos / kKvBlock < pg1) {
@@ -452,7 +463,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncthreads();
     // partial of this chunk: per head (max, sum, o[256]); a single chunk is the result itself (the combine's
     // weights would be exp(0) = 1: the same arithmetic)
-    float* part = p.part + ((((size_t)b * p.nkv + g) * p.nchunks + c) * G) * (2 + kHD);
+    float* part = p.part + ((((size_t)b * p.nkv + g) * p.nchunks + c) * G) * kPartStride;
     for (int j = 0; j < G; ++j) {
         float M = -INFINITY;
 #pragma unroll
@@ -467,7 +478,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (nce == 1) {
             const int hq = g * G + j;
-            const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);
+            float gate = 0.f;
+#pragma unroll
+            for (int q = 0; q < kMaxGroup; ++q)
+                if (q == j) gate = gin[q];
             const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(ov / Ls, sigmoid_f(gate)));
             const size_t idx = (size_t)b * p.h * kHD + hq * kHD + tid;
             reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
@@ -475,10 +489,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             continue;
         }
         if (tid == 0) {
-            part[j * (2 + kHD)] = M;
-            part[j * (2 + kHD) + 1] = Ls;
+            part[j * kPartStride] = M;
+            part[j * kPartStride + 1] = Ls;
         }
-        part[j * (2 + kHD) + 2 + tid] = ov;
+        part[j * kPartStride + 2 + tid] = ov;
     }
     if (nce == 1) return;
     // release / acquire through one thread: the barrier orders every thread's stores before thread 0's fence
@@ -493,15 +507,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     __syncthreads();
     if (!last_flag) return;
-    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate. Every load
-    // of the combine is independent, so they go out in wide rounds (each an L2 round trip): the chunks' (m, l)
-    // into shared memory in one, then each thread's dimension of every head over 8 chunks at a time.
-    const float* base = p.part + (((size_t)b * p.nkv + g) * p.nchunks) * G * (2 + kHD);
+    // combine the chunks in order: o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, then the gate.
+    const float* base = p.part + (((size_t)b * p.nkv + g) * p.nchunks) * G * kPartStride;
+    // Every load of the combine is independent, so they go out in wide rounds (each an L2 round trip): the
+    // chunks' (m, l) into shared memory in one, then each thread's dimension of every head over 8 chunks at a time.
     float* wch = reinterpret_cast<float*>(ring + kStageBytes);  // [nchunks][G] chunk maxima, then weights
     float* lch = wch + p.nchunks * G;                            // [nchunks][G] chunk sums
     for (int i = tid; i < nce * G; i += kAttnThreads) {
-        wch[i] = __ldcg(base + (size_t)i * (2 + kHD));
-        lch[i] = __ldcg(base + (size_t)i * (2 + kHD) + 1);
+        wch[i] = __ldcg(base + (size_t)i * kPartStride);
+        lch[i] = __ldcg(base + (size_t)i * kPartStride + 1);
     }
     __syncthreads();
     if (tid < G) {
@@ -527,7 +541,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int u = 0; u < kCU; ++u)
 #pragma unroll
             for (int j = 0; j < kMaxGroup; ++j)
-                ov[u][j] = (j < G && cc + u < nce) ? __ldcg(base + ((size_t)(cc + u) * G + j) * (2 + kHD) + 2 + tid) : 0.f;
+                ov[u][j] = (j < G && cc + u < nce) ? __ldcg(base + ((size_t)(cc + u) * G + j) * kPartStride + 2 + tid) : 0.f;
         // chunk weights applied in chunk order
 #pragma unroll
         for (int u = 0; u < kCU; ++u)
@@ -541,8 +555,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int j = 0; j < kMaxGroup; ++j) {
         if (j >= G) break;
         const int hq = g * G + j;
-        const float gate = __uint_as_float((uint32_t)y[p.h * kHD + hq * kHD + tid] << 16);
-        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(Ov[j] / lrow[j], sigmoid_f(gate)));
+        const __nv_bfloat16 out = __float2bfloat16_rn(mul_rn(Ov[j] / lrow[j], sigmoid_f(gin[j])));
         const size_t idx = (size_t)b * p.h * kHD + hq * kHD + tid;
         reinterpret_cast<__nv_bfloat16*>(p.o)[idx] = out;
         if (p.mixer_copy) reinterpret_cast<__nv_bfloat16*>(p.mixer_copy)[idx] = out;
@@ -552,7 +565,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 size_t attn_workspace_bytes(int nranks, int rows, int nchunks) {
     const int h = 24 / nranks, nkv = nranks <= 4 ? 4 / nranks : 1, G = h / nkv;
-    size_t part = (size_t)rows * nkv * nchunks * G * (2 + kHD) * 4;
+    size_t part = (size_t)rows * nkv * nchunks * G * kPartStride * 4;
     part = (part + 255) & ~size_t(255);
     return part + 256 + (size_t)rows * nkv * 4;
 }
@@ -632,7 +645,7 @@ cudaError_t attn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const
     p.vp = vp;
     p.o = o;
     p.mixer_copy = mixer_copy;
-    size_t part = (size_t)rows * p.nkv * nchunks * p.G * (2 + kHD) * 4;
+    size_t part = (size_t)rows * p.nkv * nchunks * p.G * kPartStride * 4;
     part = (part + 255) & ~size_t(255);
     p.part = static_cast<float*>(work);
     p.ticket = reinterpret_cast<int*>(static_cast<uint8_t*>(work) + part + 256);
