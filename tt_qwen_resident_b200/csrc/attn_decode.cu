@@ -209,7 +209,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         fence_mbar_init();
     }
     __syncthreads();
-    pdl_launch();
     if (p.pf && tid == 0) {
         const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         l2_prefetch_share(p.pf, p.pf_bytes, cta, gridDim.x * gridDim.y * gridDim.z);
@@ -443,6 +442,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (lane == 0) mbar_arrive(&empty[s]);
         }
     }
+    // the next launch (the out-projection, its weights pulled into L2 by this kernel) may start its CTAs from here
+    // on: earlier, its CTAs' start-up work on the other SMs slowed this kernel's tail
+    pdl_launch();
     // ---- merge the three groups in group order through shared memory (the ring is free: every copy landed)
     __syncthreads();
     float* mg = reinterpret_cast<float*>(ring);                 // [3][8]

@@ -79,7 +79,6 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
     __shared__ float sc[8];
     __shared__ float osq;             // this CTA's sum of o^2, read by the whole cluster
 
-    pdl_launch();
     // thread layout over the CTA's 128 x 32 slice: column quad cq (4 columns), rows 8rp .. 8rp+7
     const int cq = tid & 7, rp = tid >> 3;
     const int R = p.verify;  // verify: rows of the one user, run in order in this cluster
@@ -193,6 +192,9 @@ __global__ void __cluster_dims__(1, 1, kGdnSplit) __launch_bounds__(kGdnThreads,
                 if (which == 2 || (hh % group == 0 && qtr == 0)) hist[swr * conv + ch] = yin[it];
             }
         }
+        // the next launch may start its CTAs once this row's conv is done (earlier, their start-up work slowed
+        // this latency-bound kernel)
+        if (row == 0) pdl_launch();
         __syncthreads();
         if (!bad) {
             // ---- l2 norms of q (warps 0, 1) and k (warps 2, 3)
