@@ -174,6 +174,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_fp8_kernel(const GemvPar
     };
     if (tid == 0)
         for (int i = 0; i < min(NS, cnt); ++i) issue(i);
+    // and the ring's next fill into L2 (a prefetch, no shared destination): the stream keeps HBM busy while the
+    // prologue waits for its dependency and builds the operand, and the refills after it come from L2
+    if (tid == 0)
+        for (int i = NS; i < min(2 * NS, cnt); ++i)
+            bulk_prefetch_l2(p.w + unit_offset(u0 + i, p.tiles, nkb, nq) * kUnitBytes, kUnitBytes);
 
     pdl_wait();
     const int users = p.users;
