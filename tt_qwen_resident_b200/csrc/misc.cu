@@ -66,6 +66,47 @@ constexpr int kTopkThreads = 512;
 
 __device__ __forceinline__ uint32_t key_of_bf16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
 
+// Warp 0: scanning the 256 bins of hist from the top, the first bin b at which acc0 + (counts of bins above b) +
+// hist[b] reaches kTopK; *bin = b (-1 if the total stays below kTopK) and *above = acc0 + the counts strictly
+// above it (the total if none). Lane l holds bins 255 - 8 l .. 248 - 8 l: one scan over lanes, then the lane that
+// crosses walks its 8 bins (a serial walk over 256 bins by one thread cost microseconds).
+__device__ __forceinline__ void topk_bin(const int* hist, int acc0, int* bin, int* above) {
+    const int lane = threadIdx.x & 31;
+    int h[8], sum = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        h[q] = hist[255 - 8 * lane - q];
+        sum += h[q];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, acc0 + incl >= kTopK);
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (hit == 0u) {
+        if (lane == 0) {
+            *bin = -1;
+            *above = acc0 + total;
+        }
+        return;
+    }
+    if (lane == __ffs(hit) - 1) {
+        int a = acc0 + incl - sum;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (a + h[q] >= kTopK) {
+                *bin = 255 - 8 * lane - q;
+                *above = a;
+                return;
+            }
+            a += h[q];
+        }
+    }
+}
+
 // Select the top-32 of n candidates (key in [0, 65535], distinct indices) held in shared memory, in
 // (key desc, index asc) order, into out_k / out_i. Radix select on the 16-bit key (high byte, then low byte),
 // then the elements above the threshold plus the lowest-index ones equal to it, then a sort of those <= 32.
@@ -78,18 +119,7 @@ __device__ void block_top32(const uint16_t* keys, const uint32_t* idx, int n, ui
     __syncthreads();
     for (int i = tid; i < n; i += nt) atomicAdd(&hist[keys[i] >> 8], 1);
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0, bin = -1;
-        for (int b = 255; b >= 0; --b) {
-            if (acc + hist[b] >= kTopK) {
-                bin = b;
-                break;
-            }
-            acc += hist[b];
-        }
-        scratch[0] = bin;  // -1: fewer than 32 candidates, take all
-        scratch[1] = acc;  // count above the bin
-    }
+    if (tid < 32) topk_bin(hist, 0, &scratch[0], &scratch[1]);  // bin (-1: fewer than 32, take all), count above
     __syncthreads();
     const int hb = scratch[0];
     int T = -1;  // threshold key: everything > T is in, == T partially
@@ -99,20 +129,11 @@ __device__ void block_top32(const uint16_t* keys, const uint32_t* idx, int n, ui
         for (int i = tid; i < n; i += nt)
             if ((keys[i] >> 8) == hb) atomicAdd(&hist[keys[i] & 0xff], 1);
         __syncthreads();
-        if (tid == 0) {
-            int acc = scratch[1], lb = 0;
-            for (int b = 255; b >= 0; --b) {
-                if (acc + hist[b] >= kTopK) {
-                    lb = b;
-                    break;
-                }
-                acc += hist[b];
-            }
-            scratch[2] = (hb << 8) | lb;
-            scratch[3] = acc;  // count strictly above T
-        }
+        // the low byte's bin (-1 never happens: the high byte's bin holds the crossing) and the count strictly
+        // above T
+        if (tid < 32) topk_bin(hist, scratch[1], &scratch[2], &scratch[3]);
         __syncthreads();
-        T = scratch[2];
+        T = (hb << 8) | max(scratch[2], 0);
     }
     // gather: key > T (any order), then key == T by ascending index (block prefix over index order)
     __shared__ uint64_t cand[kTopK];
