@@ -907,6 +907,45 @@ cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, 
     return cudaLaunchKernelEx(&cfg, resid_norm_kernel, x, racc, x_out, h, rc_ranks, rc_base, rc_rem, rc_nkb, err);
 }
 
+// The down-projection's input formed once per user (4 or more rows): h = bf16(silu(g) * u) from gate|up's
+// fixed-point sums, whose rows come in quads per 4 columns c .. c+3 -- g(c), g(c+1), u(c), u(c+1), g(c+2), g(c+3),
+// u(c+2), u(c+3) -- so column quad j reads the 8 words 8 j .. 8 j + 7. The down-projection then reads its window
+// of h (PRO_BF16, 2 bytes per element and user) instead of every CTA decoding 16 bytes of sums per element and
+// user of its window (~160 KB per CTA at 8 users). Same arithmetic as the PRO_SILU_ACC prologue.
+__global__ void __launch_bounds__(256) silu_rows_kernel(const long long* acc, int ld_acc, int ic, int users, uint16_t* h) {
+    pdl_launch();
+    pdl_wait();
+    const int nq = ic / 4;
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < users * nq; i += gridDim.x * 256) {
+        const int b = i / nq, j = i - b * nq;
+        const longlong2* a = reinterpret_cast<const longlong2*>(acc + (size_t)b * ld_acc + 8 * (size_t)j);
+        const longlong2 q0 = __ldcg(a), q1 = __ldcg(a + 1), q2 = __ldcg(a + 2), q3 = __ldcg(a + 3);
+        const float g[4] = {acc_decode(q0.x), acc_decode(q0.y), acc_decode(q2.x), acc_decode(q2.y)};
+        const float u[4] = {acc_decode(q1.x), acc_decode(q1.y), acc_decode(q3.x), acc_decode(q3.y)};
+        uint32_t w[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+            w[t] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(silu_f(g[2 * t]) * u[2 * t])) |
+                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(silu_f(g[2 * t + 1]) * u[2 * t + 1])) << 16);
+        reinterpret_cast<uint2*>(h + (size_t)b * ic)[j] = make_uint2(w[0], w[1]);
+    }
+}
+
+cudaError_t silu_rows_launch(int users, const long long* acc, int ld_acc, int ic, uint16_t* h, cudaStream_t st, bool pdl) {
+    if (users < 1 || users > kMaxRows || ic % 4 || !acc || !h) return cudaErrorInvalidValue;
+    const int total = users * (ic / 4);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min((total + 255) / 256, 2 * 148));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, silu_rows_kernel, acc, ld_acc, ic, users, h);
+}
+
 // shared memory of one GEMV CTA: half an SM's (a second CTA -- the next projection's, under programmatic
 // dependent launch -- fits beside it and starts its weight stream during this one's tail); past that, up to
 // the per-CTA maximum with a shallower ring

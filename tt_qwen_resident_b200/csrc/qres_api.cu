@@ -29,6 +29,7 @@ cudaError_t gemv_launch(const qres_weight& w, int users, int pro, const void* in
 size_t gemv_workspace_bytes(int grid);
 int gemv_grid(int users, int rows_pad, int K, int grid);
 int gemv_group_blocks(int users, int epi, int K);
+cudaError_t silu_rows_launch(int users, const long long* acc, int ld_acc, int ic, uint16_t* h, cudaStream_t st, bool pdl);
 cudaError_t resid_norm_launch(int users, const float* x, const long long* racc, float* x_out, uint16_t* h,
                               cudaStream_t st, bool pdl, const GemvExchange* ex, uint32_t* err);
 cudaError_t gdn_launch(int nranks, int rows, const uint16_t* y, int ld_y, const int32_t* pos, const uint16_t* taps,
@@ -926,8 +927,13 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
                 std::swap(cur, other);
             }
             GemvExchange ed;
-            ed.gacc = accB;
-            ed.ld_gacc = 2 * c->ic;
+            if (split) {
+                // silu(g) * u formed once per user into `a` (unused on the accumulator path), read as bf16
+                STEP(silu_rows_launch(R, accB, 2 * c->ic, c->ic, c->a, st, true), "silu-mul");
+            } else {
+                ed.gacc = accB;
+                ed.ld_gacc = 2 * c->ic;
+            }
             ed.zero = XA;  // one rank: and accD, right behind it
             ed.zero_words = (size_t)R * kHidden + (tp ? 0 : (size_t)R * c->ld_y);
             if (tp) {
@@ -937,8 +943,8 @@ static qres_status enqueue_step(qres_ctx* c, cudaStream_t st) {
             } else {
                 ed.acc_out = XC;
             }
-            STEP(gemv_launch(wd, R, 3, nullptr, wd.K, tp ? 6 : 5, nullptr, kHidden, grid_of(wd), c->err, st, true, nullptr, nullptr,
-                             c->gemv_work, c->gemv_work_bytes, next_of(&wd), &ed),
+            STEP(gemv_launch(wd, R, split ? PRO_BF16 : PRO_SILU_ACC, split ? c->a : nullptr, wd.K, tp ? 6 : 5, nullptr, kHidden,
+                             grid_of(wd), c->err, st, true, nullptr, nullptr, c->gemv_work, c->gemv_work_bytes, next_of(&wd), &ed),
                  "down");
             pending_acc = producer_of(wd, XC);
             continue;
